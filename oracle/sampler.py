@@ -1,0 +1,139 @@
+"""Restatement of the WeDLM commit rule (test infrastructure only).
+
+* ``SamplingParams`` and presets      ``src/decoding/sampler.rs:12-44``, ``src/bin/cli.rs:113-137``
+* ``compute_entropies_with_probs``    ``src/decoding/sampler.rs:125-154``
+* ``sample_from_probs_at_indices``    ``src/decoding/sampler.rs:160-200`` (T = 0 branch)
+* ``select_by_entropy_with_distance`` ``src/decoding/sampler.rs:446-493``
+* streaming dynamic cap (entropy EMA) ``src/decoding/wedlm.rs:517-535``
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import List, Sequence, Tuple
+
+import numpy as np
+
+
+@dataclass
+class SamplingParams:
+    """``SamplingParams`` (``sampler.rs:12-44``); default values as ``Default``."""
+
+    temperature: float = 0.2
+    top_p: float = 1.0
+    entropy_threshold: float = 0.6
+    distance_penalty: float = 0.02
+    max_tokens_per_step: int = 4
+    margin_threshold: float = 0.0
+
+    @staticmethod
+    def preset(name: str, temperature: float = 0.0) -> "SamplingParams":
+        """``Preset::to_params`` (``cli.rs:113-137``)."""
+        table = {"quality": (0.5, 0.10, 4), "balanced": (0.8, 0.05, 8), "fast": (1.0, 0.05, 6)}
+        tau, lam, cap = table[name]
+        return SamplingParams(temperature=temperature, entropy_threshold=tau,
+                              distance_penalty=lam, max_tokens_per_step=cap)
+
+
+def scale_logits(logits: np.ndarray, temperature: float) -> np.ndarray:
+    """Logits are divided by T only when ``T > 0 && T != 1`` (``sampler.rs:127-131``)."""
+    x = np.asarray(logits, dtype=np.float32)
+    if temperature > 0.0 and temperature != 1.0:
+        x = (x / np.float32(temperature)).astype(np.float32)
+    return x
+
+
+def compute_entropies_with_probs(logits: np.ndarray, temperature: float) -> Tuple[np.ndarray, np.ndarray]:
+    """``compute_entropies_with_probs`` (``sampler.rs:125-154``).
+
+    Softmax over the (scaled) logits, then ``H = sum_{p>0} -p ln p``.  The sum is
+    accumulated in float64 here; the reference accumulates in f32, which differs
+    from the exact value by O(sqrt(V) * 2^-24) relative.
+    """
+    x = scale_logits(logits, temperature).astype(np.float64)
+    m = x.max(axis=-1, keepdims=True)
+    e = np.exp(x - m)
+    p = e / e.sum(axis=-1, keepdims=True)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        t = np.where(p > 0, -p * np.log(np.where(p > 0, p, 1.0)), 0.0)
+    H = t.sum(axis=-1).astype(np.float32)
+    return H, p.astype(np.float32)
+
+
+def row_stats(logits: np.ndarray, temperature: float):
+    """Per-row (entropy, argmax, max-prob) from the logits in one pass.
+
+    Argmax follows ``sampler.rs:183-190``: ``Iterator::max_by`` returns the LAST
+    maximum, so ties resolve to the largest index.  The max probability is
+    ``exp(x_max - m) / sum exp(x - m)``.
+    """
+    x = scale_logits(logits, temperature).astype(np.float64)
+    m = x.max(axis=-1, keepdims=True)
+    e = np.exp(x - m)
+    S = e.sum(axis=-1)
+    T = (e * x).sum(axis=-1)
+    H = (m[:, 0] + np.log(S) - T / S).astype(np.float32)
+    xr = x[:, ::-1]
+    am = (x.shape[1] - 1 - np.argmax(xr, axis=-1)).astype(np.int32)
+    maxp = (1.0 / S).astype(np.float32)
+    return H, am, maxp
+
+
+def greedy_argmax_last(probs_row: np.ndarray) -> int:
+    """T = 0 branch of ``sample_from_probs_at_indices`` (``sampler.rs:183-190``)."""
+    r = np.asarray(probs_row)
+    return int(r.shape[0] - 1 - np.argmax(r[::-1]))
+
+
+def select_by_entropy_with_distance(entropies: Sequence[float], mask_indices: Sequence[int],
+                                    entropy_threshold: float, distance_penalty: float,
+                                    max_positions: int) -> List[int]:
+    """``select_by_entropy_with_distance`` (``sampler.rs:446-493``).
+
+    ``adj_i = H_i + lambda * (pos_i - min pos)`` (f32 arithmetic); keep ``adj < tau``
+    in ascending logical position (stable sort), ``take(max_positions)``; if none,
+    the first minimum of ``adj`` in logical order.
+    """
+    if len(entropies) == 0 or len(mask_indices) == 0:
+        return []
+    leftmost = min(mask_indices)
+    lam = np.float32(distance_penalty)
+    items = []
+    for i, h in enumerate(entropies):
+        lp = mask_indices[i] if i < len(mask_indices) else i
+        dist = np.float32(max(lp - leftmost, 0))
+        adj = np.float32(np.float32(h) + np.float32(lam * dist))
+        items.append((i, lp, adj))
+    items.sort(key=lambda t: t[1])  # stable, like sort_by_key
+    tau = np.float32(entropy_threshold)
+    res = [i for (i, _, a) in items if a < tau][:max_positions]
+    if not res and items:
+        best = items[0]
+        for it in items[1:]:
+            if it[2] < best[2]:
+                best = it
+        res = [best[0]]
+    return res
+
+
+ENTROPY_EMA_ALPHA = np.float32(0.3)
+
+
+def update_running_entropy(running: float, entropies: Sequence[float]) -> np.float32:
+    """Entropy EMA (``wedlm.rs:517-522``): ``r = 0.3 * mean(H) + 0.7 * r`` in f32."""
+    if len(entropies) == 0:
+        return np.float32(running)
+    s = np.float32(0.0)
+    for h in entropies:  # sequential f32 sum, like Iterator::sum::<f32>
+        s = np.float32(s + np.float32(h))
+    avg = np.float32(s / np.float32(len(entropies)))
+    return np.float32(ENTROPY_EMA_ALPHA * avg + (np.float32(1.0) - ENTROPY_EMA_ALPHA) * np.float32(running))
+
+
+def effective_cap(running: float, tau: float, cap: int) -> int:
+    """Dynamic per-step cap (``wedlm.rs:526-535``)."""
+    r, t = np.float32(running), np.float32(tau)
+    if r < t * np.float32(0.4):
+        return cap * 2
+    if r < t * np.float32(0.7):
+        return (cap * 3 + 1) // 2
+    return cap
