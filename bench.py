@@ -1,0 +1,359 @@
+#!/usr/bin/env python3
+"""Benchmark of the WeDLM block-parallel decode step on B200.
+
+``python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+[--workload entropy_select|decode_8b]`` prints ONE JSON line (rank 0).
+
+Workloads (seeded synthetic inputs; no dataset is involved):
+
+* ``entropy_select`` -- the fused entropy-select stage at 8B vocabulary: bf16 logits
+  ``[64 x 96, 151936]`` (1.867 GB, larger than L2) drawn N(0, 2.5^2) plus one
+  N(8, 1) spike per row; tau 0.8, lambda 0.05, cap 8, T 0.  A step is one
+  ``wedlm_entropy_select`` over the whole batch.  Multi-GPU: every rank runs its own
+  batch (weak scaling, no collective on the data path).
+* ``decode_8b`` -- streaming block decode of the 8B-shape random-init bf16 model.
+
+For N > 1 launch with ``torchrun --nproc-per-node N bench.py --gpus N``.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "wedlm-rs_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "committed tok/s at 8B shape, block 96; fused entropy-select GB/s vs HBM peak"
+V_8B = 151936
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def profile_traffic(name: str):
+    """DRAM bytes per launch recorded by an ncu capture summary under profiles/."""
+    p = os.path.join(ROOT, "profiles", name)
+    try:
+        for line in open(p):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling in the background."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.samples = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append((time.time(), line.strip()))
+
+    def stop(self, t0: float, t1: float):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = [s for (t, s) in self.samples if t0 - 0.15 <= t <= t1 + 0.15] or \
+               [s for (_, s) in self.samples]
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            f = [x.strip() for x in r.split(",")]
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except (ValueError, IndexError):
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------------
+def dist_setup(gpus: int):
+    import torch
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, ws, local
+
+
+def barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, ws: int) -> float:
+    if ws == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def make_c2_logits(rows: int, V: int, seed: int):
+    import torch
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    x = torch.randn(rows, V, generator=g, device="cuda", dtype=torch.float32).mul_(2.5)
+    cols = torch.randint(0, V, (rows,), generator=g, device="cuda")
+    spike = torch.randn(rows, generator=g, device="cuda").add_(8.0)
+    x[torch.arange(rows, device="cuda"), cols] += spike
+    return x.to(torch.bfloat16)
+
+
+# ----------------------------------------------------------------------------------
+def bench_entropy_select(args, rank, ws, local):
+    import torch
+    from wedlm_b200 import Context
+    rows_per_seq, nseq = 96, args.nseq
+    rows, V = rows_per_seq * nseq, V_8B
+    ctx = Context(None, device=local)
+    logits = make_c2_logits(rows, V, seed=1234 + rank)
+    seq_rows = torch.arange(0, rows + 1, rows_per_seq, dtype=torch.int32, device="cuda")
+    mask_pos = torch.arange(rows, dtype=torch.int32, device="cuda") % rows_per_seq
+    caps = torch.full((nseq,), 8, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def step():
+        return ctx.entropy_select(logits, 0.0, 0.8, 0.05, seq_rows, mask_pos, caps, stream=stream)
+
+    nbytes = rows * V * 2
+    hbm, _, peak_kind = peaks()
+    clk = ClockSampler(local)
+    clk.start()
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    # hold the GPU under load for a while so the clock record covers a loaded period
+    t_end = time.time() + args.hold_seconds
+    while time.time() < t_end:
+        for _ in range(50):
+            step()
+        torch.cuda.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    t0 = time.time()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier(ws)
+    t1 = time.time()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    clocks = clk.stop(t0, t1)
+    ms_max = max_over_ranks(ms, ws)
+    value = nbytes * ws / (ms_max * 1e-3) / 1e9
+
+    achieved = nbytes / (ms * 1e-3) / 1e9
+    if args.profile:
+        ctx.close()
+        return {"metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": ws,
+                "ms_per_step": round(ms_max, 4), "note": "profiling run (no e2e, no clocks)"}
+
+    # end to end through the C ABI with host buffers: pinned H2D of the logits, the
+    # kernel, D2H of every per-row and per-sequence result
+    host = torch.empty((rows, V), dtype=torch.bfloat16, pin_memory=True)
+    host.copy_(logits)
+    dev = torch.empty_like(logits)
+    outs = {k: torch.empty(rows if k != "n_selected" else nseq,
+                           dtype=torch.float32 if k in ("H", "maxprob") else torch.int32,
+                           device="cuda") for k in ("H", "argmax", "maxprob", "selected", "n_selected")}
+    houts = {k: torch.empty(v.shape, dtype=v.dtype, pin_memory=True) for k, v in outs.items()}
+    d2h = sum(v.numel() * v.element_size() for v in outs.values())
+
+    def e2e_step():
+        dev.copy_(host, non_blocking=True)
+        ctx.entropy_select(dev, 0.0, 0.8, 0.05, seq_rows, mask_pos, caps, out=outs, stream=stream)
+        for k in outs:
+            houts[k].copy_(outs[k], non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(ws)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ne2e = max(3, min(args.steps, 10))
+    e0.record(stream)
+    for _ in range(ne2e):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / ne2e, ws)
+    del host, dev
+
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded N(0,2.5^2) bf16 logits + one N(8,1) spike per row",
+        "config": {"workload": f"entropy_select: {nseq} seqs x 96 mask rows x 151936 vocab, "
+                               "bf16 logits, tau 0.8, lambda 0.05, cap 8, T 0",
+                   "rows_per_gpu": rows, "vocab": V, "bytes_per_step_per_gpu": nbytes,
+                   "l2": f"inputs larger than L2 ({nbytes / 1e9:.2f} GB per GPU)",
+                   "parallelism": f"dp{ws}"},
+        "clocks": clocks,
+        "e2e": {"value": round(nbytes * ws / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": d2h},
+        "gpu_launches": args.steps,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                     "traffic": profile_traffic("entropy_select_c2.md"),
+                     "kernel": "entropy_select_kernel<bf16>"},
+    }
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_entropy(logits, budget_s=args.cpu_seconds)
+    ctx.close()
+    return line
+
+
+def cpu_baseline_entropy(logits_dev, budget_s: float, nthreads: int = 0):
+    """The C restatement of the reference's CPU path on a bounded sample (96-row
+    batches of the same logits) for about `budget_s` seconds."""
+    import numpy as np
+    import torch
+    from oracle import cbind
+    sample = logits_dev[:96].contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+    nthreads = nthreads or os.cpu_count()
+    seq_rows, mask_pos, caps = [0, 96], list(range(96)), [8]
+    cbind.entropy_select(sample, "bf16", 0.0, 0.8, 0.05, seq_rows, mask_pos, caps, nthreads)
+    n, t0 = 0, time.time()
+    while True:
+        cbind.entropy_select(sample, "bf16", 0.0, 0.8, 0.05, seq_rows, mask_pos, caps, nthreads)
+        n += 1
+        if time.time() - t0 >= budget_s:
+            break
+    dt = time.time() - t0
+    return {"value": round(n * sample.nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": nthreads,
+            "kind": "port",
+            "sample": f"{n} x 96 rows x 151936 bf16 logits (the C restatement of "
+                      f"compute_entropies_with_probs + select + greedy argmax), {dt:.1f} s"}
+
+
+def reference_entropy(args, rank, ws):
+    """--impl reference: the reference's CPU algorithm (C restatement; the Rust crate
+    cannot be built without cargo/candle) on the host cores, same metric."""
+    import numpy as np
+    from oracle import cbind
+    from oracle.model import f32_to_bf16_bits
+    rows, V = 768, V_8B
+    rng = np.random.default_rng(1234)
+    x = rng.standard_normal((rows, V), dtype=np.float32) * np.float32(2.5)
+    x[np.arange(rows), rng.integers(0, V, rows)] += rng.normal(8, 1, rows).astype(np.float32)
+    b = f32_to_bf16_bits(x)
+    nth = os.cpu_count()
+    sr = list(range(0, rows + 1, 96))
+    mp = [i % 96 for i in range(rows)]
+    caps = [8] * (rows // 96)
+    for _ in range(args.warmup):
+        cbind.entropy_select(b, "bf16", 0.0, 0.8, 0.05, sr, mp, caps, nth)
+    t0 = time.time()
+    for _ in range(args.steps):
+        cbind.entropy_select(b, "bf16", 0.0, 0.8, 0.05, sr, mp, caps, nth)
+    dt = (time.time() - t0) / args.steps
+    v = b.nbytes / dt / 1e9
+    return {"metric": METRIC, "value": round(v, 3), "unit": "GB/s", "impl": "reference",
+            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(dt * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "entropy_select: bounded sample of 8 seqs x 96 rows x 151936 "
+                                   "bf16 logits per step (same per-row work as the B200 arm)"},
+            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": nth, "kind": "port",
+                             "sample": "768 rows per step"},
+            "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+# ----------------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--workload", default="entropy_select", choices=["entropy_select"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--nseq", type=int, default=64, help="sequences of 96 mask rows per GPU")
+    ap.add_argument("--hold-seconds", type=float, default=1.0)
+    ap.add_argument("--profile", action="store_true",
+                    help="short run for ncu: no load hold, no e2e, no CPU baseline")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.profile:
+        args.hold_seconds, args.no_cpu_baseline = 0.0, True
+
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        ws = int(os.environ.get("WORLD_SIZE", "1"))
+        if rank != 0:
+            return
+        print(json.dumps(reference_entropy(args, rank, ws)), flush=True)
+        return
+
+    rank, ws, local = dist_setup(args.gpus)
+    line = bench_entropy_select(args, rank, ws, local)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -207,3 +207,26 @@ def test_streaming_commit_before_predict_and_refill():
     assert dec.trace[1].n_commit == 3
     # reordered: filled first, masks last, with true positions
     assert dec.trace[1].reordered_positions[:3] == [10, 11, 12]
+
+
+# --- the C restatement (CPU baseline / checker) against the numpy restatement ------
+def test_c_restatement_matches_numpy():
+    from oracle import cbind
+    from oracle.model import f32_to_bf16_bits, bf16_bits_to_f32
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((24, 20000), dtype=np.float32) * 2.5
+    x[3, 7] = 40.0
+    b = f32_to_bf16_bits(x)
+    mask_pos = rng.permutation(30)[:24].tolist()
+    r = cbind.entropy_select(b, "bf16", 0.0, 0.8, 0.05, [0, 10, 24], mask_pos, [8, 2])
+    H, am, _ = row_stats(bf16_bits_to_f32(b), 0.0)
+    # the reference sums p ln p sequentially in f32: ~1e-4 from the exact value here
+    assert np.abs(r["H"] - H).max() < 2e-3
+    assert (r["tokens"] == am).all()
+    for s, (r0, r1, cap) in enumerate([(0, 10, 8), (10, 24, 2)]):
+        want = select_by_entropy_with_distance(r["H"][r0:r1].tolist(), mask_pos[r0:r1], 0.8, 0.05, cap)
+        assert r["selected"][r0:r0 + r["n_selected"][s]].tolist() == want
+    # f32 input and temperature scaling
+    rf = cbind.entropy_select(x, "f32", 0.5, 0.8, 0.05, [0, 24], mask_pos, [8])
+    Hf, amf, _ = row_stats(x, 0.5)
+    assert np.abs(rf["H"] - Hf).max() < 2e-3 and (rf["tokens"] == amf).all()

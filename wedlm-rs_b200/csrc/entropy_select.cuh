@@ -1,0 +1,49 @@
+// Host-side interface of the fused entropy-select kernels (entropy_select.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace wedlm {
+
+struct EntropyArgs {
+  const void* logits = nullptr;
+  int dtype = WEDLM_BF16;
+  int rows = 0, V = 0;
+  long ld = 0;
+  float temperature = 0.f, tau = 0.f, lambda = 0.f;
+  int nseq = 0;
+  const int* seq_rows = nullptr;  // device [nseq + 1]
+  const int* mask_pos = nullptr;  // device [rows]
+  const int* caps = nullptr;      // device [nseq]
+  float* H = nullptr;
+  int* argmax = nullptr;
+  float* maxprob = nullptr;
+  int* selected = nullptr;
+  int* n_selected = nullptr;
+};
+
+// Scratch (global memory) the kernels need besides their inputs and outputs.
+struct EntropyScratch {
+  float* partials = nullptr;   // [partial_capacity] floats
+  long partial_capacity = 0;
+  float* row_H = nullptr;      // [row_capacity]
+  unsigned* row_count = nullptr;  // [row_capacity], zero between launches
+  int row_capacity = 0;
+  unsigned* seq_count = nullptr;  // [seq_capacity], zero between launches
+  int seq_capacity = 0;
+};
+
+struct EntropyPlan {
+  int splits = 1;
+  int split_cols = 0;
+};
+
+EntropyPlan plan_entropy(int rows, int V, int dtype, int num_sms);
+Status run_entropy_select(const EntropyArgs& A, const EntropyScratch& W, int num_sms,
+                          cudaStream_t st);
+Status run_entropy_partials(const EntropyArgs& A, const EntropyScratch& W, int vocab_offset,
+                            float* out, int num_sms, cudaStream_t st);
+Status run_entropy_combine(const float* partials, int nshards, const EntropyArgs& A,
+                           const EntropyScratch& W, cudaStream_t st);
+
+}  // namespace wedlm
