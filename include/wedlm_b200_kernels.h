@@ -1,0 +1,42 @@
+/*
+ * wedlm_b200_kernels.h -- kernel-level entry points of libwedlm_b200.so.
+ *
+ * These expose single kernels of the decode step for tests, profiling and callers
+ * that drive the forward pass themselves.  They have no counterpart in the reference
+ * (whose kernels are candle ops); the conventions of wedlm_b200.h apply.
+ */
+#ifndef WEDLM_B200_KERNELS_H
+#define WEDLM_B200_KERNELS_H
+
+#include "wedlm_b200.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Epilogues of wedlm_kernel_gemm. */
+enum wedlm_gemm_epilogue {
+  WEDLM_EPI_STORE = 0,       /* out = Y (model dtype)                            */
+  WEDLM_EPI_STORE_F32 = 1,   /* out = Y (f32)                                    */
+  WEDLM_EPI_RESIDUAL = 2,    /* out = resid + Y (bf16: rounded as the reference) */
+  WEDLM_EPI_SWIGLU = 3       /* out = silu(X W^T) * (X W2^T)                     */
+};
+
+/* Y[m, n] = sum_k X[m, k] * W[n, k] (Linear::forward without bias) plus epilogue.
+ * All pointers are device pointers of `dtype` (WEDLM_BF16: tcgen05 tensor cores,
+ * K % 64 == 0, 16-byte aligned rows; WEDLM_F32: CUDA cores).  Row strides are in
+ * elements.  `resid` may alias `out`. */
+WEDLM_API int wedlm_kernel_gemm(wedlm_ctx* ctx, const void* X, int64_t ldx, const void* W,
+                                const void* W2, int64_t ldw, int M, int N, int K, int dtype,
+                                int epilogue, void* out, int64_t ldo, const void* resid,
+                                int64_t ldr, void* stream);
+
+/* Synchronises `stream`, then reports (and clears) a device-side wait that gave up
+ * inside a kernel since the last check: WEDLM_ERR_TIMEOUT, else WEDLM_OK. */
+WEDLM_API int wedlm_check_device_error(wedlm_ctx* ctx, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WEDLM_B200_KERNELS_H */

@@ -253,7 +253,7 @@ class OracleModel:
 
     # -- public API mirroring causal_lm.rs --------------------------------------
     def forward_with_positions(self, input_ids, positions, kv_caches=None, rank=None,
-                               logits_rows: Optional[slice] = None):
+                               logits_rows: Optional[slice] = None, round_logits: bool = True):
         """``WeDLMForCausalLM::forward_with_positions`` (``causal_lm.rs:68-79``).
 
         Returns ``(logits [S or rows, V], new_caches)``.  ``new_caches`` holds the
@@ -274,7 +274,9 @@ class OracleModel:
         h = self._r(rms_norm(h, self.w["model.norm.weight"], self.cfg.rms_norm_eps))
         if logits_rows is not None:
             h = h[logits_rows]
-        logits = self._lin(h, "lm_head.weight")
+        logits = np.matmul(h, self.w["lm_head.weight"].T, dtype=np.float32)
+        if round_logits:
+            logits = self._r(logits)
         return logits, new
 
     def forward(self, input_ids, position_offset: int = 0, kv_caches=None):

@@ -7,12 +7,15 @@ import re
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-HEADER = os.path.join(ROOT, "include", "wedlm_b200.h")
+HEADERS = [os.path.join(ROOT, "include", h) for h in ("wedlm_b200.h", "wedlm_b200_kernels.h")]
 
 
 def header_symbols():
-    txt = open(HEADER).read()
-    return sorted(set(re.findall(r"^WEDLM_API\s+[\w\s\*]*?\b(wedlm_\w+)\s*\(", txt, re.M)))
+    syms = set()
+    for h in HEADERS:
+        txt = open(h).read()
+        syms |= set(re.findall(r"^WEDLM_API\s+[\w\s\*]*?\b(wedlm_\w+)\s*\(", txt, re.M))
+    return sorted(syms)
 
 
 def test_header_declares_entry_points():

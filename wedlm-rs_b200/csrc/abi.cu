@@ -5,6 +5,8 @@
 
 #include "context.h"
 #include "model.h"
+#include "gemm.h"
+#include "../../include/wedlm_b200_kernels.h"
 
 using wedlm::Status;
 
@@ -48,6 +50,55 @@ void free_entropy_scratch(wedlm_ctx* ctx) {
   cudaFree(W.row_count);
   cudaFree(W.seq_count);
   W = EntropyScratch{};
+}
+
+Status ensure_gemm_scratch(wedlm_ctx* ctx, long ws_floats, int counters) {
+  if (!ctx->dev_err) {
+    WEDLM_CUDA_TRY(cudaMalloc(&ctx->dev_err, sizeof(int)));
+    WEDLM_CUDA_TRY(cudaMemset(ctx->dev_err, 0, sizeof(int)));
+  }
+  if (ws_floats <= ctx->gemm_ws_floats && counters <= ctx->gemm_n_counters) return Status::ok();
+  WEDLM_CUDA_TRY(cudaDeviceSynchronize());
+  long nw = ws_floats > ctx->gemm_ws_floats ? ws_floats : ctx->gemm_ws_floats;
+  int nc = counters > ctx->gemm_n_counters ? counters : ctx->gemm_n_counters;
+  cudaFree(ctx->gemm_ws);
+  cudaFree(ctx->gemm_counters);
+  ctx->gemm_ws = nullptr;
+  ctx->gemm_counters = nullptr;
+  ctx->gemm_ws_floats = 0;
+  ctx->gemm_n_counters = 0;
+  if (nw > 0) WEDLM_CUDA_TRY(cudaMalloc(&ctx->gemm_ws, nw * sizeof(float)));
+  if (nc > 0) {
+    WEDLM_CUDA_TRY(cudaMalloc(&ctx->gemm_counters, nc * sizeof(unsigned)));
+    WEDLM_CUDA_TRY(cudaMemset(ctx->gemm_counters, 0, nc * sizeof(unsigned)));
+  }
+  ctx->gemm_ws_floats = nw;
+  ctx->gemm_n_counters = nc;
+  return Status::ok();
+}
+
+void free_gemm_scratch(wedlm_ctx* ctx) {
+  cudaFree(ctx->gemm_ws);
+  cudaFree(ctx->gemm_counters);
+  cudaFree(ctx->dev_err);
+  ctx->gemm_ws = nullptr;
+  ctx->gemm_counters = nullptr;
+  ctx->dev_err = nullptr;
+  ctx->gemm_ws_floats = 0;
+  ctx->gemm_n_counters = 0;
+}
+
+Status check_device_error(wedlm_ctx* ctx, cudaStream_t st) {
+  if (!ctx->dev_err) return Status::ok();
+  int code = 0;
+  WEDLM_CUDA_TRY(cudaMemcpyAsync(&code, ctx->dev_err, sizeof(int), cudaMemcpyDeviceToHost, st));
+  WEDLM_CUDA_TRY(cudaStreamSynchronize(st));
+  if (code != 0) {
+    cudaMemsetAsync(ctx->dev_err, 0, sizeof(int), st);
+    return Status::err(WEDLM_ERR_TIMEOUT,
+                       "a device-side wait gave up (code " + std::to_string(code) + ")");
+  }
+  return Status::ok();
 }
 
 }  // namespace wedlm
@@ -102,6 +153,7 @@ void wedlm_destroy(wedlm_ctx* ctx) {
   cudaDeviceSynchronize();
   wedlm::model_destroy(ctx);
   wedlm::free_entropy_scratch(ctx);
+  wedlm::free_gemm_scratch(ctx);
   delete ctx;
 }
 
@@ -199,3 +251,36 @@ int wedlm_entropy_combine(wedlm_ctx* ctx, const float* partials, int nshards, in
 }
 
 }  // extern "C"
+
+extern "C" int wedlm_kernel_gemm(wedlm_ctx* ctx, const void* X, int64_t ldx, const void* W,
+                                 const void* W2, int64_t ldw, int M, int N, int K, int dtype,
+                                 int epilogue, void* out, int64_t ldo, const void* resid,
+                                 int64_t ldr, void* stream) {
+  if (!ctx) return WEDLM_ERR_INVALID_ARG;
+  if (int rc = set_device(ctx)) return rc;
+  wedlm::GemmArgs a;
+  a.X = X; a.ldx = ldx; a.W = W; a.W2 = W2; a.ldw = ldw;
+  a.M = M; a.N = N; a.K = K; a.epi = epilogue;
+  a.out = out; a.ldo = ldo; a.resid = resid; a.ldr = ldr;
+  if (M <= 0 || N <= 0 || K <= 0 || !X || !W || !out || epilogue < 0 || epilogue > 3)
+    return ctx->fail(Status::err(WEDLM_ERR_INVALID_ARG, "bad GEMM arguments"));
+  cudaStream_t st = (cudaStream_t)stream;
+  Status s;
+  if (dtype == WEDLM_F32) {
+    s = wedlm::run_gemm_f32(a, st);
+  } else if (dtype == WEDLM_BF16) {
+    wedlm::GemmPlan g = wedlm::plan_gemm_tc(M, N, K, epilogue == wedlm::EPI_SWIGLU_BF16, ctx->num_sms);
+    s = wedlm::ensure_gemm_scratch(ctx, g.ws_floats, g.counters);
+    if (s.good()) s = wedlm::run_gemm_tc(a, g, ctx->gemm_ws, ctx->gemm_counters, ctx->dev_err, st);
+  } else {
+    s = Status::err(WEDLM_ERR_INVALID_ARG, "dtype must be F32 or BF16");
+  }
+  return s.good() ? WEDLM_OK : ctx->fail(s);
+}
+
+extern "C" int wedlm_check_device_error(wedlm_ctx* ctx, void* stream) {
+  if (!ctx) return WEDLM_ERR_INVALID_ARG;
+  if (int rc = set_device(ctx)) return rc;
+  wedlm::Status s = wedlm::check_device_error(ctx, (cudaStream_t)stream);
+  return s.good() ? WEDLM_OK : ctx->fail(s);
+}

@@ -1,0 +1,509 @@
+// Block attention of the reordered window against the committed-prefix KV cache, on
+// the tcgen05 tensor cores (bf16 in, f32 accumulate in TMEM).
+// Replaces softmax(QK^T / sqrt(d) + mask) V with GQA (src/model/attention.rs:188-221)
+// and the host-built causal mask (src/model/attention.rs:255-279,
+// src/model/backbone.rs:158-178): the mask is evaluated in-kernel from a per-row rank,
+// key j of the window is visible to query i iff rank[j] <= rank[i] (rank = window
+// index reproduces the reference), every cached key is visible.
+//
+// Work item = (sequence b, kv head g, 128-row query tile t, range of 128-key chunks).
+// The query tile holds the `group` q heads of kv head g for 128/group window rows, so
+// K and V of that kv head are read once for the whole group (GQA without repeat_kv).
+//   S[q][key]  = Q[q][d] . K[key][d]      A = Q   (K-major), B = K page tiles (K-major)
+//   O[q][d]   += P[q][key] . V[key][d]    A = P   (K-major), B = V^T page tiles (K-major,
+//                                          the cache stores V transposed within a page)
+// Both accumulators have TMEM lane = query row, so the thread that owns a query row does
+// its online softmax, rescales its O row when the running max grows, and writes it out.
+// Warp roles: warp 0 TMA producer (Q once, K/V chunks through a 2-stage ring), warp 1
+// TMEM allocator + MMA issuer, warps 2..5 softmax / correction / epilogue.
+// A work item covering only part of the keys writes (m, l, O) partials; a combine
+// kernel merges them (flash-decoding split-KV).
+#include <cudaTypedefs.h>
+
+#include <cfloat>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "layer_ops.h"
+#include "sm100.cuh"
+
+namespace wedlm {
+
+Status make_tmap(CUtensorMap* m, const void* base, long rows, long cols, long ld, int box_rows);
+
+namespace {
+
+using namespace sm100;
+
+constexpr int kThreadsAT = 192;
+constexpr int kQT = 128;        // query rows per tile
+constexpr int kKC = 128;        // keys per chunk (two 64-key pages)
+constexpr int kD = 128;         // head dim (this kernel)
+constexpr int kBlk = 128 * 128; // bytes of one [128 rows x 64 bf16] K-block
+constexpr int kStages = 2;
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct AttnWork {
+  int b, g, t, c0, c1, split;  // chunk range [c0, c1)
+  int part;                    // partial slot, -1 = final output written directly
+};
+
+struct AtParams {
+  int rows, nh, nkv, group, page_size, pages_per_seq, num_pages, layer;
+  const int* page_table;
+  const int* row_seq;
+  const int* seq_row0;
+  const int* seq_rows;
+  const int* seq_cache_len;
+  const int* seq_slot;
+  const int* rank;
+  const AttnWork* work;
+  __nv_bfloat16* out;
+  long ld_out;
+  float* part_o;   // [parts][128][128]
+  float* part_ml;  // [parts][128][2]
+  float scale_log2;
+  int* err;
+};
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15]))
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// byte offset of element (row, col) in a 128-byte-swizzled [rows x 64] bf16 K-block
+__device__ __forceinline__ uint32_t sw128_off(int row, int col) {
+  const int chunk = (col >> 3) ^ (row & 7);
+  return (uint32_t)(row * 128 + chunk * 16 + (col & 7) * 2);
+}
+
+__global__ void __launch_bounds__(kThreadsAT, 1)
+attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const AtParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  // layout: Q (2 blocks) | stage s: K (2 blocks), V (2 blocks) | P (2 blocks) | barriers
+  uint8_t* sQ = smem;
+  uint8_t* sKV = sQ + 2 * kBlk;
+  uint8_t* sP = sKV + kStages * 4 * kBlk;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kBlk);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = kv_full + kStages;
+  uint64_t* s_full = kv_empty + kStages;
+  uint64_t* p_full = s_full + 1;
+  uint64_t* o_done = p_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 1);
+  int* s_rank = reinterpret_cast<int*>(tmem_slot + 4);  // window ranks of sequence b
+
+  const AttnWork w = p.work[blockIdx.x];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = w.b, g = w.g;
+  const int row0 = p.seq_row0[b], S = p.seq_rows[b], L = p.seq_cache_len[b];
+  const int slot = p.seq_slot[b];
+  const int nchunks = w.c1 - w.c0;
+
+  for (int j = threadIdx.x; j < S; j += blockDim.x) s_rank[j] = p.rank ? p.rank[row0 + j] : j;
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(kv_full + s, 1);
+      mbar_init(kv_empty + s, 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 1);
+    mbar_init(o_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 256);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tO = tmem + 128;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      // Q tile: rows (g * rows + row0) * group + t * 128 of the group-major q buffer
+      const int qrow = (g * p.rows + row0) * p.group + w.t * kQT;
+      mbar_arrive_expect_tx(q_full, 2 * kBlk);
+      tma_load_2d(sQ, &tmQ, q_full, 0, qrow);
+      tma_load_2d(sQ + kBlk, &tmQ, q_full, 64, qrow);
+      int issued = 0;
+      for (int i = 0; i < nchunks; ++i) {
+        const int s = i % kStages;
+        const uint32_t ph = (uint32_t)(i / kStages) & 1u;
+        if (!mbar_wait(kv_empty + s, ph ^ 1u, p.err, kErrWaitEmpty)) break;
+        issued = i + 1;
+        uint8_t* st = sKV + s * 4 * kBlk;
+        mbar_arrive_expect_tx(kv_full + s, 4 * kBlk);
+        const int c = w.c0 + i;
+        for (int pg = 0; pg < 2; ++pg) {
+          const int page = p.page_table[(long)slot * p.pages_per_seq + 2 * c + pg];
+          const int krow = ((p.layer * p.num_pages + page) * p.nkv + g) * p.page_size;
+          // K: two d-halves (K-blocks), keys of page pg at rows 64 * pg
+          tma_load_2d(st + pg * (kBlk / 2), &tmK, kv_full + s, 0, krow);
+          tma_load_2d(st + kBlk + pg * (kBlk / 2), &tmK, kv_full + s, 64, krow);
+          // V^T page: [128 d rows x 64 keys] = K-block pg of the B operand
+          const int vrow = ((p.layer * p.num_pages + page) * p.nkv + g) * kD;
+          tma_load_2d(st + 2 * kBlk + pg * kBlk, &tmV, kv_full + s, 0, vrow);
+        }
+      }
+      mbar_wait(q_full, 0, p.err, kErrWaitDrain);
+      for (int s = 0; s < kStages && s < issued; ++s) {
+        const int last = s + ((issued - 1 - s) / kStages) * kStages;
+        mbar_wait(kv_full + s, (uint32_t)(last / kStages) & 1u, p.err, kErrWaitDrain);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      const uint32_t idesc = idesc_bf16_f32(128, 128);
+      const uint32_t aq = smem_u32(sQ), ap = smem_u32(sP);
+      bool ok = mbar_wait(q_full, 0, p.err, kErrWaitFull);
+      for (int i = 0; i < nchunks && ok; ++i) {
+        const int s = i % kStages;
+        if (!mbar_wait(kv_full + s, (uint32_t)(i / kStages) & 1u, p.err, kErrWaitFull)) break;
+        tc_fence_after();
+        const uint32_t bk = smem_u32(sKV + s * 4 * kBlk);
+        if (i > 0) {
+          // O += P(i-1) . V(i-1)
+          if (!mbar_wait(p_full, (uint32_t)(i - 1) & 1u, p.err, kErrWaitFull)) break;
+          tc_fence_after();
+          const int sp = (i - 1) % kStages;
+          const uint32_t bv = smem_u32(sKV + sp * 4 * kBlk + 2 * kBlk);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            tc_mma_f16(tO, smem_desc_sw128(ap + (kk >> 2) * kBlk + (kk & 3) * 32),
+                       smem_desc_sw128(bv + (kk >> 2) * kBlk + (kk & 3) * 32), idesc,
+                       (i - 1) > 0 || kk > 0);
+          tc_commit(o_done);
+          tc_commit(kv_empty + sp);
+        }
+        // S = Q . K(i)^T
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          tc_mma_f16(tS, smem_desc_sw128(aq + (kk >> 2) * kBlk + (kk & 3) * 32),
+                     smem_desc_sw128(bk + (kk >> 2) * kBlk + (kk & 3) * 32), idesc, kk > 0);
+        tc_commit(s_full);
+      }
+      if (ok && nchunks > 0 && mbar_wait(p_full, (uint32_t)(nchunks - 1) & 1u, p.err, kErrWaitFull)) {
+        tc_fence_after();
+        const int sp = (nchunks - 1) % kStages;
+        const uint32_t bv = smem_u32(sKV + sp * 4 * kBlk + 2 * kBlk);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          tc_mma_f16(tO, smem_desc_sw128(ap + (kk >> 2) * kBlk + (kk & 3) * 32),
+                     smem_desc_sw128(bv + (kk >> 2) * kBlk + (kk & 3) * 32), idesc,
+                     (nchunks - 1) > 0 || kk > 0);
+      }
+      tc_commit(o_done);
+      tc_commit(kv_empty + ((nchunks > 0 ? nchunks - 1 : 0) % kStages));
+    }
+  } else {
+    // ---------------- softmax / correction / epilogue (warps 2..5) ----------------
+    const int q4 = warp & 3;
+    const int qr = q4 * 32 + lane;                 // query row within the tile (TMEM lane)
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const int qi = w.t * kQT + qr;                 // query index within (b, g)
+    const bool qvalid = qi < S * p.group;
+    const int r_local = qvalid ? qi / p.group : 0;
+    const int my_rank = s_rank[r_local];
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int i = 0; i < nchunks && ok; ++i) {
+      ok = mbar_wait(s_full, (uint32_t)i & 1u, p.err, kErrWaitAccum);
+      tc_fence_after();
+      const int kbase = (w.c0 + i) * kKC;
+      // pass 1: masked row max (scores in log2 units)
+      float cm = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 8; ++c) {
+        float v[16];
+        tmem_ld16(tS + lane_off + c * 16, v);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int kp = kbase + c * 16 + j;
+          bool vis = kp < L;
+          if (!vis && kp < L + S) vis = s_rank[kp - L] <= my_rank;
+          if (vis) cm = fmaxf(cm, v[j] * p.scale_log2);
+        }
+      }
+      const float mn = fmaxf(m, cm);
+      const float base = mn == -INFINITY ? 0.f : mn;
+      float ps = 0.f;
+      // PV(i-1) must be complete before P is overwritten and O is rescaled
+      if (i > 0) ok = ok && mbar_wait(o_done, (uint32_t)(i - 1) & 1u, p.err, kErrWaitAccum);
+      tc_fence_after();
+      // pass 2: P = 2^(s - max) as bf16 into the swizzled K-major P tile
+#pragma unroll 1
+      for (int c = 0; c < 8; ++c) {
+        float v[16];
+        tmem_ld16(tS + lane_off + c * 16, v);
+        uint32_t pk[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float e2[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int kp = kbase + c * 16 + 2 * j + u;
+            bool vis = kp < L;
+            if (!vis && kp < L + S) vis = s_rank[kp - L] <= my_rank;
+            e2[u] = vis ? fast_exp2(v[2 * j + u] * p.scale_log2 - base) : 0.f;
+          }
+          const __nv_bfloat162 h2 = __floats2bfloat162_rn(e2[0], e2[1]);
+          ps += __low2float(h2) + __high2float(h2);
+          pk[j] = *reinterpret_cast<const uint32_t*>(&h2);
+        }
+        const int key0 = c * 16;
+        const int blk = key0 >> 6, col = key0 & 63;
+        uint8_t* prow = sP + blk * kBlk;
+        *reinterpret_cast<uint4*>(prow + sw128_off(qr, col)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        *reinterpret_cast<uint4*>(prow + sw128_off(qr, col + 8)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+      }
+      if (i > 0 && mn > m && m != -INFINITY) {
+        const float f = fast_exp2(m - mn);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          float v[16];
+          tmem_ld16(tO + lane_off + c * 16, v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] *= f;
+          tmem_st16(tO + lane_off + c * 16, v);
+        }
+      }
+      l = (m == -INFINITY ? 0.f : l * fast_exp2(m - base)) + ps;
+      m = mn;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      named_bar_sync(1, 128);
+      if (warp == 2 && lane == 0) mbar_arrive(p_full);
+    }
+    ok = ok && mbar_wait(o_done, (uint32_t)(nchunks > 0 ? nchunks - 1 : 0) & 1u, p.err,
+                         kErrWaitAccum);
+    tc_fence_after();
+    const int r = row0 + r_local;
+    const int h = g * p.group + (qi % p.group);
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll 1
+    for (int c = 0; c < 8; ++c) {
+      float v[16];
+      tmem_ld16(tO + lane_off + c * 16, v);
+      if (!(ok && qvalid)) continue;
+      if (w.part < 0) {
+        __nv_bfloat16* dst = p.out + (long)r * p.ld_out + (long)h * kD + c * 16;
+        uint32_t pk[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * j] * inv, v[2 * j + 1] * inv);
+          pk[j] = *reinterpret_cast<const uint32_t*>(&h2);
+        }
+        *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        *reinterpret_cast<uint4*>(dst + 8) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+      } else {
+        float* po = p.part_o + ((long)w.part * kQT + qr) * kD + c * 16;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          *reinterpret_cast<float4*>(po + 4 * j) = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      }
+    }
+    if (ok && qvalid && w.part >= 0) {
+      p.part_ml[((long)w.part * kQT + qr) * 2] = m;
+      p.part_ml[((long)w.part * kQT + qr) * 2 + 1] = l;
+    }
+    tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// Merge the split-KV partials of one (b, g, t) tile: one warp per query row.
+struct CombineItem {
+  int b, g, t, part0, nparts;
+};
+
+__global__ void attention_combine_kernel(const CombineItem* items, int nitems, AtParams p) {
+  const int wid = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (wid >= nitems * kQT) return;
+  const CombineItem it = items[wid / kQT];
+  const int qr = wid % kQT;
+  const int S = p.seq_rows[it.b];
+  const int qi = it.t * kQT + qr;
+  if (qi >= S * p.group) return;
+  float M = -INFINITY;
+  for (int k = 0; k < it.nparts; ++k) {
+    const float* ml = p.part_ml + ((long)(it.part0 + k) * kQT + qr) * 2;
+    if (ml[1] > 0.f) M = fmaxf(M, ml[0]);
+  }
+  float acc[4] = {0.f, 0.f, 0.f, 0.f}, lsum = 0.f;
+  for (int k = 0; k < it.nparts; ++k) {
+    const long pi = (long)(it.part0 + k) * kQT + qr;
+    const float mk = p.part_ml[pi * 2], lk = p.part_ml[pi * 2 + 1];
+    if (!(lk > 0.f)) continue;
+    const float f = fast_exp2(mk - M);
+    lsum += f * lk;
+    const float4 v = *reinterpret_cast<const float4*>(p.part_o + pi * kD + lane * 4);
+    acc[0] += f * v.x;
+    acc[1] += f * v.y;
+    acc[2] += f * v.z;
+    acc[3] += f * v.w;
+  }
+  const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+  const int r = p.seq_row0[it.b] + qi / p.group;
+  const int h = it.g * p.group + qi % p.group;
+  __nv_bfloat16* dst = p.out + (long)r * p.ld_out + (long)h * kD + lane * 4;
+  const __nv_bfloat162 a = __floats2bfloat162_rn(acc[0] * inv, acc[1] * inv);
+  const __nv_bfloat162 c = __floats2bfloat162_rn(acc[2] * inv, acc[3] * inv);
+  uint2 pk;
+  pk.x = *reinterpret_cast<const uint32_t*>(&a);
+  pk.y = *reinterpret_cast<const uint32_t*>(&c);
+  *reinterpret_cast<uint2*>(dst) = pk;
+}
+
+}  // namespace
+
+// ---- host: plan once per forward, run once per layer ------------------------------------
+// Workspace layout (floats): [AttnWork table | CombineItem table | part_o | part_ml].
+long attention_ws_floats(const AttnArgs& a) {
+  const long tiles = (long)a.nkv * (((long)a.rows * a.group + kQT - 1) / kQT + a.nseq);
+  const long chunks = (a.max_kv + kKC - 1) / kKC + 1;
+  const long items = tiles * chunks;
+  return items * 8 + items * 6 + items * (long)kQT * (kD + 2) + 1024;
+}
+
+Status plan_attention_tc(const AttnArgs& a, const int* h_seq_rows, const int* h_cache_len,
+                         int num_sms, float* ws, long ws_floats, void* h_staging,
+                         size_t staging_bytes, AttnPlan* plan, cudaStream_t st) {
+  WEDLM_CHECK_ARG(a.head_dim == kD, "tensor-core attention needs head_dim 128");
+  WEDLM_CHECK_ARG(a.page_size == 64, "tensor-core attention needs 64-token pages");
+  WEDLM_CHECK_ARG(kQT % a.group == 0, "query tile must hold whole GQA groups");
+  std::vector<AttnWork> work;
+  std::vector<CombineItem> comb;
+  long base = 0;
+  for (int b = 0; b < a.nseq; ++b) {
+    WEDLM_CHECK_ARG(h_seq_rows[b] <= 4096, "window longer than 4096 rows");
+    base += (long)a.nkv * ((h_seq_rows[b] * a.group + kQT - 1) / kQT);
+  }
+  const long target = 2L * num_sms;
+  int part = 0;
+  for (int b = 0; b < a.nseq; ++b) {
+    const int S = h_seq_rows[b], L = h_cache_len[b];
+    if (S == 0) continue;
+    const int tiles = (S * a.group + kQT - 1) / kQT;
+    const int chunks = (L + S + kKC - 1) / kKC;
+    int splits = base > 0 ? (int)((target + base - 1) / base) : 1;
+    splits = splits < 1 ? 1 : (splits > chunks ? chunks : splits);
+    for (int g = 0; g < a.nkv; ++g)
+      for (int t = 0; t < tiles; ++t) {
+        if (splits > 1) comb.push_back(CombineItem{b, g, t, part, splits});
+        for (int s2 = 0; s2 < splits; ++s2) {
+          AttnWork w;
+          w.b = b;
+          w.g = g;
+          w.t = t;
+          w.c0 = (int)((long)chunks * s2 / splits);
+          w.c1 = (int)((long)chunks * (s2 + 1) / splits);
+          w.split = s2;
+          w.part = splits > 1 ? part++ : -1;
+          work.push_back(w);
+        }
+      }
+  }
+  plan->n_work = (int)work.size();
+  plan->n_comb = (int)comb.size();
+  if (work.empty()) return Status::ok();
+  const long need = (long)work.size() * 8 + (long)comb.size() * 6 + 4 + (long)part * kQT * (kD + 2);
+  WEDLM_CHECK_ARG(need <= ws_floats, "attention workspace too small");
+  // the combine table starts 8 floats per work item into the workspace
+  static_assert(sizeof(AttnWork) <= 8 * sizeof(float), "AttnWork slot");
+  static_assert(sizeof(CombineItem) <= 6 * sizeof(float), "CombineItem slot");
+  const size_t wbytes = work.size() * sizeof(AttnWork), cbytes = comb.size() * sizeof(CombineItem);
+  const size_t coff = work.size() * 8 * sizeof(float);
+  WEDLM_CHECK_ARG(coff + cbytes <= staging_bytes, "attention staging too small");
+  uint8_t* hs = reinterpret_cast<uint8_t*>(h_staging);
+  memcpy(hs, work.data(), wbytes);
+  memcpy(hs + coff, comb.data(), cbytes);
+  WEDLM_CUDA_TRY(cudaMemcpyAsync(ws, hs, coff + cbytes, cudaMemcpyHostToDevice, st));
+  plan->work = ws;
+  plan->comb = ws + work.size() * 8;
+  float* po = ws + work.size() * 8 + comb.size() * 6;
+  po = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(po) + 15) & ~uintptr_t(15));
+  plan->part_o = po;
+  plan->part_ml = po + (long)part * kQT * kD;
+  return Status::ok();
+}
+
+Status run_attention_tc(const AttnArgs& a, const AttnPlan& plan, int* err, cudaStream_t st) {
+  if (plan.n_work == 0) return Status::ok();
+  CUtensorMap mQ, mK, mV;
+  WEDLM_TRY(make_tmap(&mQ, a.q, (long)a.nkv * a.rows * a.group, kD, kD, kQT));
+  WEDLM_TRY(make_tmap(&mK, a.kcache, (long)a.num_layers * a.num_pages * a.nkv * a.page_size, kD, kD, 64));
+  WEDLM_TRY(make_tmap(&mV, a.vcache, (long)a.num_layers * a.num_pages * a.nkv * kD, a.page_size,
+                      a.page_size, kD));
+  AtParams p;
+  p.rows = a.rows;
+  p.nh = a.nh;
+  p.nkv = a.nkv;
+  p.group = a.group;
+  p.page_size = a.page_size;
+  p.pages_per_seq = a.pages_per_seq;
+  p.num_pages = a.num_pages;
+  p.layer = a.layer;
+  p.page_table = a.page_table;
+  p.row_seq = a.row_seq;
+  p.seq_row0 = a.seq_row0;
+  p.seq_rows = a.seq_rows;
+  p.seq_cache_len = a.seq_cache_len;
+  p.seq_slot = a.seq_slot;
+  p.rank = a.rank;
+  p.work = reinterpret_cast<const AttnWork*>(plan.work);
+  p.out = reinterpret_cast<__nv_bfloat16*>(a.out);
+  p.ld_out = a.ld_out;
+  p.part_o = plan.part_o;
+  p.part_ml = plan.part_ml;
+  p.scale_log2 = kLog2e / sqrtf((float)kD);
+  p.err = err;
+  const size_t smem = 1024 + (2 + kStages * 4 + 2) * kBlk + 16 * 8 + 4096 * 4;
+  int dev = 0;
+  WEDLM_CUDA_TRY(cudaGetDevice(&dev));
+  static unsigned attr_set = 0;
+  if (dev < 32 && !(attr_set & (1u << dev))) {
+    WEDLM_CUDA_TRY(cudaFuncSetAttribute(attention_tc_kernel,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr_set |= 1u << dev;
+  }
+  attention_tc_kernel<<<(unsigned)plan.n_work, kThreadsAT, smem, st>>>(mQ, mK, mV, p);
+  WEDLM_CUDA_TRY(cudaGetLastError());
+  if (plan.n_comb > 0) {
+    const long warps = (long)plan.n_comb * kQT;
+    attention_combine_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(
+        reinterpret_cast<const CombineItem*>(plan.comb), plan.n_comb, p);
+    WEDLM_CUDA_TRY(cudaGetLastError());
+  }
+  return Status::ok();
+}
+
+}  // namespace wedlm

@@ -9,6 +9,10 @@
 #include "common.cuh"
 #include "entropy_select.cuh"
 
+namespace wedlm {
+struct ModelState;
+}
+
 struct wedlm_ctx {
   int device = 0;
   int num_sms = 148;
@@ -20,8 +24,15 @@ struct wedlm_ctx {
 
   wedlm::EntropyScratch ent{};
 
-  // model state lives in ModelState (model.cu); opaque here
-  struct ModelState* model = nullptr;
+  // split-K GEMM workspace and the device error word of the bounded waits
+  float* gemm_ws = nullptr;
+  long gemm_ws_floats = 0;
+  unsigned* gemm_counters = nullptr;
+  int gemm_n_counters = 0;
+  int* dev_err = nullptr;
+
+  // model state (model.cu); opaque here
+  wedlm::ModelState* model = nullptr;
 
   int fail(const wedlm::Status& s) {
     last_error = s.msg;
@@ -35,5 +46,10 @@ namespace wedlm {
 // partial words.  Synchronises the device when it reallocates.
 Status ensure_entropy_scratch(wedlm_ctx* ctx, int rows, int nseq, long partial_floats);
 void free_entropy_scratch(wedlm_ctx* ctx);
+// Grow the split-K workspace / tile counters (synchronises when it reallocates).
+Status ensure_gemm_scratch(wedlm_ctx* ctx, long ws_floats, int counters);
+void free_gemm_scratch(wedlm_ctx* ctx);
+// Read and clear the device error word; a non-zero code means a bounded wait gave up.
+Status check_device_error(wedlm_ctx* ctx, cudaStream_t st);
 
 }  // namespace wedlm

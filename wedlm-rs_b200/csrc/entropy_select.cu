@@ -197,7 +197,8 @@ __device__ __forceinline__ Acc load_partial(const float* p) {
 __device__ void finalize_sequence(int b, int r0, int r1, const float* part, long rs, long ks,
                                   int nk, float tau, float lambda, const int* __restrict__ mask_pos,
                                   const int* __restrict__ caps, float* row_H, float* H,
-                                  int* argmax, float* maxprob, int* selected, int* n_selected) {
+                                  int* argmax, float* maxprob, int* selected, int* n_selected,
+                                  float* running) {
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
   const int M = r1 - r0;
   for (int r = r0 + w; r < r1; r += kThreads / 32) {
@@ -236,8 +237,25 @@ __device__ void finalize_sequence(int b, int r0, int r1, const float* part, long
   }
   __syncthreads();
   const int leftmost = sh_i[0];
+  __shared__ int sh_cap;
+  if (threadIdx.x == 0) {
+    int cap0 = caps[b];
+    if (running != nullptr && M > 0) {
+      // entropy EMA and dynamic cap, f32 in the reference's operation order
+      // (wedlm.rs:517-535): sequential sum, mean, 0.3 * mean + (1 - 0.3) * r
+      float sum = 0.f;
+      for (int i = 0; i < M; ++i) sum = __fadd_rn(sum, __ldcg(row_H + r0 + i));
+      const float mean = __fdiv_rn(sum, (float)M);
+      const float a = 0.3f;
+      const float r = __fadd_rn(__fmul_rn(a, mean), __fmul_rn(__fsub_rn(1.f, a), running[b]));
+      running[b] = r;
+      if (r < __fmul_rn(tau, 0.4f)) cap0 = cap0 * 2;
+      else if (r < __fmul_rn(tau, 0.7f)) cap0 = (cap0 * 3 + 1) / 2;
+    }
+    sh_cap = cap0;
+  }
   __syncthreads();
-  const int cap = caps[b];
+  const int cap = sh_cap;
   int npass = 0;
   float best_adj = FLT_MAX;
   int best_rank = INT_MAX, best_i = -1;
@@ -326,7 +344,7 @@ entropy_select_kernel(const T* __restrict__ logits, int V, long ld, int splits, 
                       int nseq, const int* __restrict__ seq_rows, const int* __restrict__ mask_pos,
                       const int* __restrict__ caps, float tau, float lambda,
                       float* __restrict__ row_H, float* H, int* argmax, float* maxprob,
-                      int* selected, int* n_selected) {
+                      int* selected, int* n_selected, float* running) {
   const int row = blockIdx.x / splits;
   const int split = blockIdx.x - row * splits;
   const int c0 = split * split_cols;
@@ -361,7 +379,7 @@ entropy_select_kernel(const T* __restrict__ logits, int V, long ld, int splits, 
   __threadfence();
   const int b = s_seq;
   finalize_sequence(b, seq_rows[b], seq_rows[b + 1], part, splits, 1, splits, tau, lambda,
-                    mask_pos, caps, row_H, H, argmax, maxprob, selected, n_selected);
+                    mask_pos, caps, row_H, H, argmax, maxprob, selected, n_selected, running);
   if (threadIdx.x == 0) seq_count[b] = 0u;
 }
 
@@ -406,10 +424,10 @@ __global__ void __launch_bounds__(kThreads)
 entropy_combine_kernel(const float* __restrict__ part, int nshards, int rows, const int* seq_rows,
                        const int* mask_pos, const int* caps, float tau, float lambda,
                        float* row_H, float* H, int* argmax, float* maxprob, int* selected,
-                       int* n_selected) {
+                       int* n_selected, float* running) {
   const int b = blockIdx.x;
   finalize_sequence(b, seq_rows[b], seq_rows[b + 1], part, 1, rows, nshards, tau, lambda,
-                    mask_pos, caps, row_H, H, argmax, maxprob, selected, n_selected);
+                    mask_pos, caps, row_H, H, argmax, maxprob, selected, n_selected, running);
 }
 
 int pick_splits(int rows, int V, int num_sms) {
@@ -430,12 +448,12 @@ void launch_select(const EntropyArgs& A, const EntropyScratch& W, int splits, in
     entropy_select_kernel<T, true><<<grid, kThreads, 0, st>>>(
         (const T*)A.logits, A.V, A.ld, splits, split_cols, invT, W.partials, W.seq_count, A.nseq,
         A.seq_rows, A.mask_pos, A.caps, A.tau, A.lambda, W.row_H, A.H, A.argmax, A.maxprob,
-        A.selected, A.n_selected);
+        A.selected, A.n_selected, A.running);
   else
     entropy_select_kernel<T, false><<<grid, kThreads, 0, st>>>(
         (const T*)A.logits, A.V, A.ld, splits, split_cols, invT, W.partials, W.seq_count, A.nseq,
         A.seq_rows, A.mask_pos, A.caps, A.tau, A.lambda, W.row_H, A.H, A.argmax, A.maxprob,
-        A.selected, A.n_selected);
+        A.selected, A.n_selected, A.running);
 }
 
 template <typename T>
@@ -524,7 +542,7 @@ Status run_entropy_combine(const float* partials, int nshards, const EntropyArgs
   entropy_combine_kernel<<<A.nseq, kThreads, 0, st>>>(partials, nshards, A.rows, A.seq_rows,
                                                       A.mask_pos, A.caps, A.tau, A.lambda, W.row_H,
                                                       A.H, A.argmax, A.maxprob, A.selected,
-                                                      A.n_selected);
+                                                      A.n_selected, A.running);
   WEDLM_CUDA_TRY(cudaGetLastError());
   return Status::ok();
 }

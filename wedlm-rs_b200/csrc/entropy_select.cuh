@@ -15,6 +15,10 @@ struct EntropyArgs {
   const int* seq_rows = nullptr;  // device [nseq + 1]
   const int* mask_pos = nullptr;  // device [rows]
   const int* caps = nullptr;      // device [nseq]
+  // Optional streaming-decode mode (wedlm.rs:517-535): when `running` is set, each
+  // sequence's entropy EMA running[b] is updated with the mean entropy of its rows and
+  // the cap becomes the dynamic cap derived from caps[b] (the preset cap).
+  float* running = nullptr;       // device [nseq]
   float* H = nullptr;
   int* argmax = nullptr;
   float* maxprob = nullptr;

@@ -1,0 +1,535 @@
+// tcgen05 / TMEM GEMM for the projections of the decode step (bf16 in, f32 accumulate):
+//   Y[tok, n] = sum_k X[tok, k] * W[n, k]      (Linear::forward, x W^T, no bias)
+// Replaces the candle matmuls behind q/k/v/o (src/model/attention.rs:145-147,229),
+// gate/up/down (src/model/mlp.rs:40-44) and the LM head (src/model/causal_lm.rs:77).
+//
+// Swap-AB: the MMA's M = 128 covers weight rows and its N covers the token rows of the
+// step (96 for one block-96 window), so at batch 1 the tensor core's M side is filled
+// with weights, which are what streams from HBM.  The fused gate/up projection keeps
+// two accumulators side by side in TMEM and applies SwiGLU in the epilogue.
+//
+// Stream-K persistent schedule: the iteration space (tile, 64-wide k-block) is cut into
+// one contiguous range per SM, so every SM streams the same number of weight bytes
+// whatever the tile count (no wave quantisation).  A tile covered by one CTA is written
+// directly by its epilogue; each CTA publishes the f32 partials of the (at most two)
+// tiles it shares with neighbours, and a small follow-up kernel sums every shared tile
+// in CTA order (deterministic) and applies the epilogue.
+// Warp roles:
+//   warp 0        TMA producer: weight / activation tiles (128-byte swizzle) into a ring
+//                 of shared-memory stages, completion on "full" mbarriers;
+//   warp 1        TMEM allocator and MMA issuer (one thread): 4 MMAs of K = 16 per stage,
+//                 tcgen05.commit frees the stage; double-buffered accumulators;
+//   warps 2..5    epilogue: tcgen05.ld (one weight row per thread), residual / SwiGLU,
+//                 bf16 or f32 stores, or partial publication for shared tiles.
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <tuple>
+
+#include "gemm.h"
+#include "sm100.cuh"
+
+namespace wedlm {
+
+namespace {
+
+using namespace sm100;
+
+constexpr int kThreadsTC = 192;
+constexpr int kBK = 64;              // K elements per stage (128 bytes of bf16)
+constexpr int kTileN = 128;          // weight rows per tile (MMA M)
+constexpr int kATileBytes = kTileN * kBK * 2;
+
+struct TcParams {
+  int N, M, K;
+  int n_tiles, t_tiles, kb_total;
+  long iters;          // tiles * kb_total
+  int grid;
+  int tok_tile;
+  int epi, dual;
+  int stages, nbuf;
+  uint32_t stage_bytes, tmem_cols, acc_cols;
+  void* out;
+  int ldo;
+  const __nv_bfloat16* resid;
+  int ldr;
+  float* ws;           // [grid][2 slots][na][tok_tile][128 weight rows]
+  int* err;
+  int vec_ok;          // out / resid rows 16-byte aligned
+};
+
+__device__ __forceinline__ long range_start(long c, long iters, int grid) {
+  return c * iters / grid;
+}
+// the CTA whose range holds iteration x: max c with floor(c*I/G) <= x == ceil((x+1)G/I) - 1
+__device__ __forceinline__ int owner_cta(long x, long iters, int grid) {
+  long c = ((x + 1) * grid + iters - 1) / iters - 1;
+  return (int)(c < 0 ? 0 : (c >= grid ? grid - 1 : c));
+}
+
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__device__ __forceinline__ void epilogue_store(const TcParams& p, int tok, int n, float a, float a2) {
+  switch (p.epi) {
+    case EPI_STORE_F32:
+      reinterpret_cast<float*>(p.out)[(long)tok * p.ldo + n] = a;
+      break;
+    case EPI_RESID_BF16: {
+      // reference: residual + bf16(projection), rounded to bf16 (layer.rs:72,78)
+      float r = __bfloat162float(p.resid[(long)tok * p.ldr + n]);
+      reinterpret_cast<__nv_bfloat16*>(p.out)[(long)tok * p.ldo + n] =
+          __float2bfloat16_rn(r + bf16r(a));
+      break;
+    }
+    case EPI_SWIGLU_BF16: {
+      // reference: silu(bf16 gate) * bf16 up, each op rounded to bf16 (mlp.rs:40-43)
+      float g = bf16r(a), u = bf16r(a2);
+      float s = bf16r(g / (1.f + __expf(-g)));
+      reinterpret_cast<__nv_bfloat16*>(p.out)[(long)tok * p.ldo + n] = __float2bfloat16_rn(s * u);
+      break;
+    }
+    default:
+      reinterpret_cast<__nv_bfloat16*>(p.out)[(long)tok * p.ldo + n] = __float2bfloat16_rn(a);
+  }
+}
+
+// Epilogue for NV consecutive weight rows n .. n+NV-1 of one token (NV = 8 or 16):
+// 16-byte vector stores when the row span is in bounds and aligned.
+template <int NV>
+__device__ __forceinline__ void epilogue_store_vec(const TcParams& p, int tok, int n,
+                                                   const float* a, const float* a2) {
+  if (!p.vec_ok || n + NV > p.N) {
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+      if (n + k < p.N) epilogue_store(p, tok, n + k, a[k], p.dual ? a2[k] : 0.f);
+    return;
+  }
+  if (p.epi == EPI_STORE_F32) {
+    float* dst = reinterpret_cast<float*>(p.out) + (long)tok * p.ldo + n;
+#pragma unroll
+    for (int k = 0; k < NV; k += 4)
+      *reinterpret_cast<float4*>(dst + k) = make_float4(a[k], a[k + 1], a[k + 2], a[k + 3]);
+    return;
+  }
+  float y[NV];
+  if (p.epi == EPI_RESID_BF16) {
+    const __nv_bfloat16* rs = p.resid + (long)tok * p.ldr + n;
+#pragma unroll
+    for (int k = 0; k < NV; k += 8) {
+      const uint4 rv = *reinterpret_cast<const uint4*>(rs + k);
+      const uint32_t w[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        y[k + 2 * u] = bf16_lo(w[u]) + bf16r(a[k + 2 * u]);
+        y[k + 2 * u + 1] = bf16_hi(w[u]) + bf16r(a[k + 2 * u + 1]);
+      }
+    }
+  } else if (p.epi == EPI_SWIGLU_BF16) {
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const float g = bf16r(a[k]), u = bf16r(a2[k]);
+      y[k] = bf16r(g / (1.f + __expf(-g))) * u;
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < NV; ++k) y[k] = a[k];
+  }
+  __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + (long)tok * p.ldo + n;
+#pragma unroll
+  for (int k = 0; k < NV; k += 8) {
+    uint32_t w[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const __nv_bfloat162 h2 = __floats2bfloat162_rn(y[k + 2 * u], y[k + 2 * u + 1]);
+      w[u] = *reinterpret_cast<const uint32_t*>(&h2);
+    }
+    *reinterpret_cast<uint4*>(dst + k) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+struct Seg {
+  long it0, it1;  // global iteration range of this segment
+  int tile;
+  bool full;      // covers the whole tile
+};
+
+__device__ __forceinline__ Seg segment_at(long it, long end, int kb_total) {
+  Seg s;
+  s.tile = (int)(it / kb_total);
+  const long tile_end = (long)(s.tile + 1) * kb_total;
+  s.it0 = it;
+  s.it1 = end < tile_end ? end : tile_end;
+  s.full = (it == (long)s.tile * kb_total) && (s.it1 == tile_end);
+  return s;
+}
+
+__global__ void __launch_bounds__(kThreadsTC, 1)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmW2,
+               const __grid_constant__ CUtensorMap tmX, const TcParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.stages * p.stage_bytes);
+  uint64_t* empty = full + p.stages;
+  uint64_t* acc_full = empty + p.stages;   // [2]
+  uint64_t* acc_empty = acc_full + 2;      // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  // per-epilogue-warp transpose buffers: [2 accumulators][16 tokens][33]
+  float* tbuf = reinterpret_cast<float*>(smem + p.stages * p.stage_bytes + 1024);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cta = blockIdx.x;
+  const long beg = range_start(cta, p.iters, p.grid);
+  const long end = range_start(cta + 1, p.iters, p.grid);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full + b, 1);
+      mbar_init(acc_empty + b, 1);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, p.tmem_cols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      tma_prefetch_desc(&tmW);
+      tma_prefetch_desc(&tmX);
+      if (p.dual) tma_prefetch_desc(&tmW2);
+      const uint64_t pol_w = policy_evict_first();
+      const uint32_t a_bytes = kATileBytes * (p.dual ? 2 : 1);
+      long issued = 0;
+      for (long it = beg; it < end; ++it) {
+        const long i = it - beg;
+        const int s = (int)(i % p.stages);
+        const uint32_t ph = (uint32_t)(i / p.stages) & 1u;
+        if (!mbar_wait(empty + s, ph ^ 1u, p.err, kErrWaitEmpty)) break;
+        issued = i + 1;
+        const int tile = (int)(it / p.kb_total), kb = (int)(it % p.kb_total);
+        const int n0 = (tile / p.t_tiles) * kTileN, t0 = (tile % p.t_tiles) * p.tok_tile;
+        uint8_t* st = smem + s * p.stage_bytes;
+        mbar_arrive_expect_tx(full + s, p.stage_bytes);
+        tma_load_2d_hint(st, &tmW, full + s, kb * kBK, n0, pol_w);
+        if (p.dual) tma_load_2d_hint(st + kATileBytes, &tmW2, full + s, kb * kBK, n0, pol_w);
+        tma_load_2d(st + a_bytes, &tmX, full + s, kb * kBK, t0);
+      }
+      // drain: wait for the last load issued to every stage before the CTA may exit
+      for (long s = 0; s < p.stages && s < issued; ++s) {
+        const long last = s + ((issued - 1 - s) / p.stages) * p.stages;
+        mbar_wait(full + s, (uint32_t)(last / p.stages) & 1u, p.err, kErrWaitDrain);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      const uint32_t idesc = idesc_bf16_f32(kTileN, p.tok_tile);
+      const uint32_t a_bytes = kATileBytes * (p.dual ? 2 : 1);
+      bool ok = true;
+      int nseg = 0;
+      for (long it = beg; it < end && ok;) {
+        const Seg sg = segment_at(it, end, p.kb_total);
+        const int buf = nseg % p.nbuf;
+        const uint32_t use = (uint32_t)(nseg / p.nbuf);
+        // wait until the epilogue has drained this accumulator buffer
+        if (!mbar_wait(acc_empty + buf, (use & 1u) ^ 1u, p.err, kErrWaitAccumEmpty)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + (uint32_t)(buf * p.acc_cols);
+        for (long j = sg.it0; j < sg.it1; ++j) {
+          const long i = j - beg;
+          const int s = (int)(i % p.stages);
+          if (!mbar_wait(full + s, (uint32_t)(i / p.stages) & 1u, p.err, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * p.stage_bytes);
+          const uint32_t sb = sa + a_bytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const bool accum = (j != sg.it0) || (kk != 0);
+            const uint64_t bd = smem_desc_sw128(sb + kk * 32);
+            tc_mma_f16(acc, smem_desc_sw128(sa + kk * 32), bd, idesc, accum);
+            if (p.dual)
+              tc_mma_f16(acc + (uint32_t)p.tok_tile, smem_desc_sw128(sa + kATileBytes + kk * 32),
+                         bd, idesc, accum);
+          }
+          tc_commit(empty + s);
+        }
+        tc_commit(acc_full + buf);
+        it = sg.it1;
+        ++nseg;
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int q = warp & 3;
+    const int na = p.dual ? 2 : 1;
+    const long slot_floats = (long)na * p.tok_tile * kTileN;
+    int nseg = 0;
+    for (long it = beg; it < end;) {
+      const Seg sg = segment_at(it, end, p.kb_total);
+      const int buf = nseg % p.nbuf;
+      const uint32_t use = (uint32_t)(nseg / p.nbuf);
+      const bool ok = mbar_wait(acc_full + buf, use & 1u, p.err, kErrWaitAccum);
+      tc_fence_after();
+      const uint32_t trow = tmem + (uint32_t)(buf * p.acc_cols) + ((uint32_t)(q * 32) << 16);
+      const int n0 = (sg.tile / p.t_tiles) * kTileN, t0 = (sg.tile % p.t_tiles) * p.tok_tile;
+      const int tok_end = min(p.tok_tile, p.M - t0);
+      // shared tile: publish this CTA's partial in slot 0 (its first segment) or slot 1
+      // (its last), layout [na][tok_tile][128 weight rows] f32; the reduce kernel sums
+      // the contributors of every shared tile.
+      const int slot = (sg.it0 == beg) ? 0 : 1;
+      float* part = p.ws + ((long)cta * 2 + slot) * slot_floats;
+      float* tb = tbuf + (warp - 2) * (2 * 16 * 33);
+      const int jt = lane >> 1, hh = (lane & 1) * 16;   // transposed view: token, row half
+      for (int c = 0; c < p.tok_tile; c += 16) {
+        float v[16], v2[16];
+        tmem_ld16(trow + (uint32_t)c, v);
+        if (p.dual) tmem_ld16(trow + (uint32_t)(p.tok_tile + c), v2);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          tb[j * 33 + lane] = v[j];
+          if (p.dual) tb[16 * 33 + j * 33 + lane] = v2[j];
+        }
+        __syncwarp();
+        float o[16], o2[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          o[k] = tb[jt * 33 + hh + k];
+          o2[k] = p.dual ? tb[16 * 33 + jt * 33 + hh + k] : 0.f;
+        }
+        __syncwarp();
+        const int rr = q * 32 + hh;  // first of this lane's 16 weight rows in the tile
+        if (sg.full) {
+          if (ok && c + jt < tok_end) epilogue_store_vec<16>(p, t0 + c + jt, n0 + rr, o, o2);
+        } else {
+          float* dst = part + (long)(c + jt) * kTileN + rr;
+#pragma unroll
+          for (int k = 0; k < 16; k += 4)
+            *reinterpret_cast<float4*>(dst + k) = make_float4(o[k], o[k + 1], o[k + 2], o[k + 3]);
+          if (p.dual) {
+            float* dst2 = part + (long)(p.tok_tile + c + jt) * kTileN + rr;
+#pragma unroll
+            for (int k = 0; k < 16; k += 4)
+              *reinterpret_cast<float4*>(dst2 + k) = make_float4(o2[k], o2[k + 1], o2[k + 2], o2[k + 3]);
+          }
+        }
+      }
+      tc_fence_before();
+      named_bar_sync(1, 128);
+      if (warp == 2 && lane == 0) mbar_arrive(acc_empty + buf);
+      it = sg.it1;
+      ++nseg;
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, p.tmem_cols);
+  }
+}
+
+// Sum the partials of every tile shared by several CTAs, in CTA order, and apply the
+// epilogue.  CTA c (1 <= c < grid) owns the tile holding range boundary start(c) when
+// that boundary is not a tile edge and no smaller boundary falls inside the same tile.
+__global__ void __launch_bounds__(256) gemm_reduce_kernel(const TcParams p) {
+  const int c = blockIdx.x + 1;
+  const long x = range_start(c, p.iters, p.grid);
+  if (x % p.kb_total == 0) return;
+  const int tile = (int)(x / p.kb_total);
+  const long x0 = (long)tile * p.kb_total, x1 = x0 + p.kb_total;
+  if (c > 1) {
+    const long xp = range_start(c - 1, p.iters, p.grid);
+    if (xp > x0) return;  // an earlier boundary lies inside this tile
+  }
+  const int cf = owner_cta(x0, p.iters, p.grid);
+  const int cl = owner_cta(x1 - 1, p.iters, p.grid);
+  const int na = p.dual ? 2 : 1;
+  const long slot_floats = (long)na * p.tok_tile * kTileN;
+  const int n0 = (tile / p.t_tiles) * kTileN, t0 = (tile % p.t_tiles) * p.tok_tile;
+  const int tok_end = min(p.tok_tile, p.M - t0);
+  for (int e = threadIdx.x; e < tok_end * (kTileN / 8); e += blockDim.x) {
+    const int tok = e / (kTileN / 8), r8 = (e % (kTileN / 8)) * 8;
+    float a[8] = {0, 0, 0, 0, 0, 0, 0, 0}, a2[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int k = cf; k <= cl; ++k) {
+      const int sl = range_start(k, p.iters, p.grid) < x0 ? 1 : 0;
+      const float* src = p.ws + ((long)k * 2 + sl) * slot_floats + (long)tok * kTileN + r8;
+#pragma unroll
+      for (int u = 0; u < 8; u += 4) {
+        const float4 f = __ldcg(reinterpret_cast<const float4*>(src + u));
+        a[u] += f.x; a[u + 1] += f.y; a[u + 2] += f.z; a[u + 3] += f.w;
+        if (p.dual) {
+          const float4 f2 = __ldcg(reinterpret_cast<const float4*>(src + (long)p.tok_tile * kTileN + u));
+          a2[u] += f2.x; a2[u + 1] += f2.y; a2[u + 2] += f2.z; a2[u + 3] += f2.w;
+        }
+      }
+    }
+    epilogue_store_vec<8>(p, t0 + tok, n0 + r8, a, a2);
+  }
+}
+
+// ---- host: tensor maps ---------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+struct TmapCache {
+  std::mutex mu;
+  std::map<std::tuple<const void*, long, long, long, int>, CUtensorMap> maps;
+};
+TmapCache& tmap_cache() {
+  static TmapCache c;
+  return c;
+}
+
+}  // namespace
+
+// bf16 row-major [rows, cols] with row stride ld (elements); box = box_rows x 64 columns.
+Status make_tmap(CUtensorMap* m, const void* base, long rows, long cols, long ld, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return Status::err(WEDLM_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  WEDLM_CHECK_ARG(((uintptr_t)base & 15) == 0, "TMA base address must be 16-byte aligned");
+  WEDLM_CHECK_ARG((ld * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return Status::err(WEDLM_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+  return Status::ok();
+}
+
+Status cached_tmap(CUtensorMap* out, const void* base, long rows, long cols, long ld, int box_rows) {
+  TmapCache& c = tmap_cache();
+  std::lock_guard<std::mutex> lk(c.mu);
+  auto key = std::make_tuple(base, rows, cols, ld, box_rows);
+  auto it = c.maps.find(key);
+  if (it != c.maps.end()) {
+    *out = it->second;
+    return Status::ok();
+  }
+  CUtensorMap m;
+  WEDLM_TRY(make_tmap(&m, base, rows, cols, ld, box_rows));
+  if (c.maps.size() > 4096) c.maps.clear();
+  c.maps.emplace(key, m);
+  *out = m;
+  return Status::ok();
+}
+
+void forget_tensor_maps() {
+  TmapCache& c = tmap_cache();
+  std::lock_guard<std::mutex> lk(c.mu);
+  c.maps.clear();
+}
+
+GemmPlan plan_gemm_tc(int M, int N, int K, bool dual, int num_sms) {
+  GemmPlan g;
+  int tt = ((M + 15) / 16) * 16;
+  if (tt > 256 || (dual && tt > 128)) {
+    const int cap = dual ? 128 : 256;
+    const int nt = (M + cap - 1) / cap;
+    tt = ((M + nt - 1) / nt + 15) / 16 * 16;
+  }
+  g.tok_tile = tt < 16 ? 16 : tt;
+  g.t_tiles = (M + g.tok_tile - 1) / g.tok_tile;
+  g.n_tiles = (N + kTileN - 1) / kTileN;
+  g.kb_total = K / kBK;
+  const long iters = (long)g.n_tiles * g.t_tiles * g.kb_total;
+  g.grid = (int)(iters < num_sms ? iters : num_sms);
+  g.splits = 1;
+  g.stage_bytes = (uint32_t)(kATileBytes * (dual ? 2 : 1) + g.tok_tile * kBK * 2);
+  const uint32_t budget = 192 * 1024;
+  int st = (int)(budget / g.stage_bytes);
+  g.stages = st > 8 ? 8 : (st < 2 ? 2 : st);
+  g.acc_cols = (uint32_t)(g.tok_tile * (dual ? 2 : 1));
+  g.nbuf = g.acc_cols * 2 <= 512 ? 2 : 1;
+  uint32_t tc = 32;
+  while (tc < g.acc_cols * g.nbuf) tc <<= 1;
+  g.tmem_cols = tc;
+  // stages | barriers (<= 1 KB) | epilogue transpose buffers (4 warps x 2 x 16 x 33 f32)
+  g.smem_bytes = 1024 + g.stages * g.stage_bytes + 1024 + 4 * 2 * 16 * 33 * 4;
+  g.ws_floats = (long)g.grid * 2 * (dual ? 2 : 1) * g.tok_tile * kTileN;
+  g.counters = 0;
+  return g;
+}
+
+Status run_gemm_tc(const GemmArgs& a, const GemmPlan& g, float* ws, unsigned* counters, int* err,
+                   cudaStream_t st) {
+  WEDLM_CHECK_ARG(a.K % kBK == 0, "tcgen05 GEMM needs K % 64 == 0");
+  WEDLM_CHECK_ARG(a.M > 0 && a.N > 0, "empty GEMM");
+  WEDLM_CHECK_ARG(ws != nullptr, "the GEMM needs its workspace");
+  (void)counters;
+  const bool dual = a.epi == EPI_SWIGLU_BF16;
+  WEDLM_CHECK_ARG(!dual || a.W2, "SwiGLU GEMM needs the second weight matrix");
+  CUtensorMap mW, mW2, mX;
+  WEDLM_TRY(cached_tmap(&mW, a.W, a.N, a.K, a.ldw, kTileN));
+  WEDLM_TRY(cached_tmap(&mW2, dual ? a.W2 : a.W, a.N, a.K, a.ldw, kTileN));
+  WEDLM_TRY(cached_tmap(&mX, a.X, a.M, a.K, a.ldx, g.tok_tile));
+  TcParams p;
+  p.N = a.N;
+  p.M = a.M;
+  p.K = a.K;
+  p.n_tiles = g.n_tiles;
+  p.t_tiles = g.t_tiles;
+  p.kb_total = g.kb_total;
+  p.iters = (long)g.n_tiles * g.t_tiles * g.kb_total;
+  p.grid = g.grid;
+  p.tok_tile = g.tok_tile;
+  p.epi = a.epi;
+  p.dual = dual ? 1 : 0;
+  p.stages = g.stages;
+  p.nbuf = g.nbuf;
+  p.stage_bytes = g.stage_bytes;
+  p.tmem_cols = g.tmem_cols;
+  p.acc_cols = g.acc_cols;
+  p.out = a.out;
+  p.ldo = (int)a.ldo;
+  p.resid = reinterpret_cast<const __nv_bfloat16*>(a.resid);
+  p.ldr = (int)a.ldr;
+  p.ws = ws;
+  p.err = err;
+  const int osz = a.epi == EPI_STORE_F32 ? 4 : 2;
+  p.vec_ok = ((uintptr_t)a.out % 16 == 0) && ((a.ldo * osz) % 16 == 0) &&
+             (a.epi != EPI_RESID_BF16 || (((uintptr_t)a.resid % 16 == 0) && (a.ldr * 2) % 16 == 0));
+  int dev = 0;
+  WEDLM_CUDA_TRY(cudaGetDevice(&dev));
+  static unsigned attr_set = 0;  // one bit per device
+  if (dev < 32 && !(attr_set & (1u << dev))) {
+    WEDLM_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        227 * 1024));
+    attr_set |= 1u << dev;
+  }
+  gemm_tc_kernel<<<(unsigned)g.grid, kThreadsTC, g.smem_bytes, st>>>(mW, mW2, mX, p);
+  WEDLM_CUDA_TRY(cudaGetLastError());
+  if (g.grid > 1) {
+    gemm_reduce_kernel<<<(unsigned)(g.grid - 1), 256, 0, st>>>(p);
+    WEDLM_CUDA_TRY(cudaGetLastError());
+  }
+  return Status::ok();
+}
+
+}  // namespace wedlm

@@ -1,0 +1,72 @@
+// Host interface of the decoder-layer kernels (layer_ops.cu, attention_tc.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace wedlm {
+
+// Paged KV cache geometry, shared by the append and attention kernels.
+//   K: [layers][num_pages][nkv][page_size][d]
+//   V: [layers][num_pages][nkv][d][page_size]   (transposed within a page)
+struct KvGeom {
+  void* kcache = nullptr;
+  void* vcache = nullptr;
+  const int* page_table = nullptr;  // [seqs][pages_per_seq]
+  int pages_per_seq = 0, num_pages = 0, page_size = 64;
+  int layer = 0, num_layers = 1;
+};
+
+struct RopeKvArgs : KvGeom {
+  const void* qkv = nullptr;  // [rows, ld_qkv]: q heads, then k heads, then v heads
+  long ld_qkv = 0;
+  int rows = 0, nh = 0, nkv = 0, group = 1, head_dim = 0;
+  int qk_norm = 1;
+  const float* q_norm = nullptr;
+  const float* k_norm = nullptr;
+  float eps = 1e-6f;
+  const int* positions = nullptr;  // [rows] RoPE position of each row
+  const float* cos = nullptr;      // [max_pos, d/2]
+  const float* sin = nullptr;
+  const int* row_seq = nullptr;    // [rows] cache slot (sequence) of each row
+  const int* dst_pos = nullptr;    // [rows] cache position written by each row
+  void* q_out = nullptr;           // group-major [nkv][rows * group][d]
+};
+
+struct AttnArgs : KvGeom {
+  const void* q = nullptr;  // group-major [nkv][rows * group][d]
+  int rows = 0, nh = 0, nkv = 0, group = 1, head_dim = 0;
+  const int* row_seq = nullptr;        // [rows] batch index b of each row
+  const int* seq_row0 = nullptr;       // [nseq] first row of sequence b
+  const int* seq_rows = nullptr;       // [nseq] rows (window length S_b) of sequence b
+  const int* seq_cache_len = nullptr;  // [nseq] committed cache length L_b
+  const int* seq_slot = nullptr;       // [nseq] cache slot (page-table row) of sequence b
+  const int* rank = nullptr;           // [rows] mask rank, NULL = index within window
+  void* out = nullptr;                 // [rows, ld_out] (head h at column h * d)
+  long ld_out = 0;
+  int nseq = 0, max_kv = 0;            // max_kv = max_b (L_b + S_b)
+};
+
+Status run_embed(const void* table, int dtype, const int* ids, int rows, int H, int vocab,
+                 void* out, int* err, cudaStream_t st);
+Status run_rmsnorm(const void* x, long ldx, const float* w, int rows, int H, float eps, int dtype,
+                   void* out, long ldo, cudaStream_t st);
+Status run_rope_kv(const RopeKvArgs& a, int dtype, cudaStream_t st);
+Status run_attention_f32(const AttnArgs& a, cudaStream_t st);
+
+// bf16 block attention on the tensor cores.  The plan (work items, split-KV layout) is
+// built once per forward from host copies of the per-sequence window and cache lengths
+// and uploaded into the workspace `ws`; run_attention_tc is then called per layer.
+struct AttnPlan {
+  int n_work = 0, n_comb = 0;
+  const float* work = nullptr;
+  const float* comb = nullptr;
+  float* part_o = nullptr;
+  float* part_ml = nullptr;
+};
+long attention_ws_floats(const AttnArgs& a);
+Status plan_attention_tc(const AttnArgs& a, const int* h_seq_rows, const int* h_cache_len,
+                         int num_sms, float* ws, long ws_floats, void* h_staging,
+                         size_t staging_bytes, AttnPlan* plan, cudaStream_t st);
+Status run_attention_tc(const AttnArgs& a, const AttnPlan& plan, int* err, cudaStream_t st);
+
+}  // namespace wedlm

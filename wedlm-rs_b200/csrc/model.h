@@ -1,11 +1,83 @@
 // Model state: weights, paged KV cache, activation buffers and the forward pass.
 #pragma once
 
+#include <vector>
+
 #include "context.h"
+#include "gemm.h"
+#include "layer_ops.h"
 
 namespace wedlm {
 
+struct LayerWeights {
+  void* wqkv = nullptr;   // [q_dim + 2 kv_dim, H]: q_proj rows, then k_proj, then v_proj
+  void* wo = nullptr;     // [H, q_dim]
+  void* wgate = nullptr;  // [I, H]
+  void* wup = nullptr;    // [I, H]
+  void* wdown = nullptr;  // [H, I]
+  float* ln1 = nullptr;   // input_layernorm [H]
+  float* ln2 = nullptr;   // post_attention_layernorm [H]
+  float* qn = nullptr;    // q_norm [d]
+  float* kn = nullptr;    // k_norm [d]
+};
+
+// One sequence's slice of a forward: `rows` window tokens written at cache slot `slot`
+// starting at its committed length; logits for window rows [logit_begin, rows).
+struct SeqSlice {
+  int slot = 0;
+  int rows = 0;
+  int logit_begin = 0;
+};
+
+struct ModelState {
+  wedlm_config cfg{};
+  int dt = WEDLM_BF16, esz = 2;
+  int H = 0, I = 0, V = 0, nh = 0, nkv = 0, d = 0, group = 1, nlayers = 0;
+  int qdim = 0, kvdim = 0, qkvdim = 0;
+  int vlo = 0, vhi = 0, vshard = 0;
+  float eps = 1e-6f;
+
+  uint8_t* arena = nullptr;  // every weight in one allocation
+  size_t arena_bytes = 0;
+  void* embed = nullptr;
+  void* lm_head = nullptr;
+  float* final_norm = nullptr;
+  std::vector<LayerWeights> layers;
+  float* cos = nullptr;  // [max_pos, d/2] (rounded to the model dtype, rope.rs:94-95)
+  float* sin = nullptr;
+
+  // paged KV cache: K [L][pages][nkv][page][d], V [L][pages][nkv][d][page]
+  int page_size = 64, pages_per_seq = 0, num_pages = 0, max_seqs = 0, max_ctx = 0;
+  void* kcache = nullptr;
+  void* vcache = nullptr;
+  int* page_table = nullptr;
+  std::vector<int> cache_len;     // committed length per slot
+  std::vector<int> pending_rows;  // rows written by the last forward, per slot
+
+  // activations, capacity max_rows token rows
+  int max_rows = 0;
+  void *h = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr,
+       *act = nullptr, *xl = nullptr;
+  // per-forward metadata (device) and its pinned host staging
+  int* d_meta = nullptr;
+  int* h_meta = nullptr;
+  size_t meta_ints = 0;
+  float* attn_ws = nullptr;
+  long attn_ws_floats = 0;
+  void* h_attn_staging = nullptr;
+  size_t attn_staging_bytes = 0;
+  cudaStream_t stream = nullptr;  // internal stream (NULL-stream calls use it)
+};
+
 Status model_create(wedlm_ctx* ctx, const wedlm_config& cfg, int max_seqs, int max_ctx);
 void model_destroy(wedlm_ctx* ctx);
+
+// Forward of a batch of windows.  tokens / positions / rank are host arrays over all
+// rows (sequence-major).  Writes the window K/V at each slot's committed length (not
+// committed) and, when logits != NULL, the logits of every sequence's rows
+// [logit_begin, rows) densely to logits ([n, vshard], dtype logits_dtype).
+Status model_forward(wedlm_ctx* ctx, const std::vector<SeqSlice>& seqs, const int* tokens,
+                     const int* positions, const int* rank, void* logits, int logits_dtype,
+                     int* n_logit_rows, cudaStream_t st);
 
 }  // namespace wedlm

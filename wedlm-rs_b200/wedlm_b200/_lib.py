@@ -77,6 +77,10 @@ _PROTOS = {
                                            C.POINTER(WedlmBlockStats), P]),
     "wedlm_generate_streaming_batch": (C.c_int, [P, C.c_int, P, C.c_int, C.c_int, C.c_int,
                                                  C.POINTER(WedlmSamplingParams), P, P, P, P]),
+    # kernel-level entry points (include/wedlm_b200_kernels.h)
+    "wedlm_kernel_gemm": (C.c_int, [P, P, C.c_int64, P, P, C.c_int64, C.c_int, C.c_int, C.c_int,
+                                    C.c_int, C.c_int, P, C.c_int64, P, C.c_int64, P]),
+    "wedlm_check_device_error": (C.c_int, [P, P]),
 }
 
 _lib = None
@@ -115,5 +119,7 @@ def ptr(t) -> C.c_void_p:
 
 def stream_ptr(stream=None) -> C.c_void_p:
     import torch
+    if stream == 0:
+        return None
     s = stream if stream is not None else torch.cuda.current_stream()
     return C.c_void_p(s.cuda_stream)

@@ -174,3 +174,139 @@ class Context:
                                          stream_ptr(stream))
         check(rc, self.h)
         return out
+
+    # ---- kernel-level entry points ------------------------------------------------------
+    EPI_STORE, EPI_STORE_F32, EPI_RESIDUAL, EPI_SWIGLU = 0, 1, 2, 3
+
+    def gemm(self, X, W, out, epilogue: int = 0, W2=None, resid=None, stream=None):
+        """``out[m, n] (epilogue)= sum_k X[m, k] W[n, k]`` through ``wedlm_kernel_gemm``."""
+        import torch
+        M, K = X.shape
+        N = W.shape[0]
+        dt = BF16 if X.dtype == torch.bfloat16 else F32
+        rc = lib().wedlm_kernel_gemm(self.h, ptr(X), X.stride(0), ptr(W), ptr(W2), W.stride(0),
+                                     M, N, K, dt, epilogue, ptr(out), out.stride(0), ptr(resid),
+                                     resid.stride(0) if resid is not None else 0,
+                                     stream_ptr(stream))
+        check(rc, self.h)
+        return out
+
+    def check_device_error(self, stream=None):
+        check(lib().wedlm_check_device_error(self.h, stream_ptr(stream)), self.h)
+
+    # ---- model: weights ---------------------------------------------------------------
+    def set_weight(self, name: str, array) -> None:
+        """Upload one checkpoint tensor (numpy f32 / f16, or uint16 bf16 bit patterns
+        with ``bf16=True`` semantics via dtype uint16)."""
+        import numpy as np
+        a = np.ascontiguousarray(array)
+        if a.dtype == np.float32:
+            dt = F32
+        elif a.dtype == np.float16:
+            dt = 2
+        elif a.dtype == np.uint16:
+            dt = BF16
+        else:
+            a = np.ascontiguousarray(a, dtype=np.float32)
+            dt = F32
+        shape = (C.c_int64 * a.ndim)(*a.shape)
+        check(lib().wedlm_set_weight(self.h, name.encode(), a.ctypes.data, dt, shape, a.ndim),
+              self.h)
+
+    def load_weights(self, weights: dict) -> None:
+        for k, v in weights.items():
+            self.set_weight(k, v)
+
+    def init_random(self, seed: int = 0, std: float = 0.02) -> None:
+        check(lib().wedlm_init_random(self.h, seed, std), self.h)
+
+    def get_weight(self, name: str, shape):
+        """Stored tensor in the model dtype (bf16 returned as uint16 bit patterns;
+        norm weights as f32)."""
+        import numpy as np
+        is_norm = name.endswith("norm.weight")
+        dt = np.float32 if (is_norm or self.config.dtype_code == F32) else np.uint16
+        out = np.empty(shape, dtype=dt)
+        check(lib().wedlm_get_weight(self.h, name.encode(), out.ctypes.data, out.nbytes), self.h)
+        return out
+
+    # ---- model: KV cache ----------------------------------------------------------------
+    def reset_sequence(self, seq: int = 0) -> None:
+        check(lib().wedlm_reset_sequence(self.h, seq), self.h)
+
+    def cache_len(self, seq: int = 0) -> int:
+        v = C.c_int32()
+        check(lib().wedlm_cache_len(self.h, seq, C.byref(v)), self.h)
+        return v.value
+
+    def commit(self, seq: int, n_commit: int) -> None:
+        check(lib().wedlm_commit(self.h, seq, n_commit), self.h)
+
+    def truncate(self, seq: int, new_len: int) -> None:
+        check(lib().wedlm_truncate(self.h, seq, new_len), self.h)
+
+    def prefill(self, seq: int, ids, stream=None) -> None:
+        import numpy as np
+        a = np.ascontiguousarray(ids, dtype=np.int32)
+        check(lib().wedlm_prefill(self.h, seq, a.ctypes.data, a.size, stream_ptr(stream)),
+              self.h)
+
+    # ---- model: forward -------------------------------------------------------------------
+    def forward_with_positions(self, seqs, tokens, positions, rank=None, logit_row_begin=None,
+                               logits_dtype=None, stream=None):
+        """``WeDLMForCausalLM::forward_with_positions`` for ``len(seqs)`` windows of equal
+        length S (``tokens`` / ``positions`` / ``rank``: int arrays ``[nseq, S]``).
+        Returns the logits of rows ``logit_row_begin[b]:S`` of every window, packed, as a
+        CUDA tensor (model dtype unless ``logits_dtype`` is torch.float32)."""
+        import numpy as np
+        import torch
+        seqs = np.ascontiguousarray(np.atleast_1d(seqs), dtype=np.int32)
+        tok = np.ascontiguousarray(np.atleast_2d(tokens), dtype=np.int32)
+        pos = np.ascontiguousarray(np.atleast_2d(positions), dtype=np.int32)
+        nseq, S = tok.shape
+        rk = None if rank is None else np.ascontiguousarray(np.atleast_2d(rank), dtype=np.int32)
+        lb = np.zeros(nseq, np.int32) if logit_row_begin is None else \
+            np.ascontiguousarray(np.atleast_1d(logit_row_begin), dtype=np.int32)
+        nrows = int(sum(S - int(b) for b in lb))
+        V = (self.config.vocab_shard_end - self.config.vocab_shard_begin) or self.config.vocab_size
+        model_dt = torch.float32 if self.config.dtype_code == F32 else torch.bfloat16
+        tdt = logits_dtype or model_dt
+        logits = torch.empty(max(nrows, 1), V, dtype=tdt, device=f"cuda:{self.device}")
+        n = C.c_int32()
+        check(lib().wedlm_block_forward(self.h, nseq, seqs.ctypes.data, tok.ctypes.data,
+                                        pos.ctypes.data, rk.ctypes.data if rk is not None else None,
+                                        S, lb.ctypes.data, ptr(logits),
+                                        F32 if tdt == torch.float32 else BF16, C.byref(n),
+                                        stream_ptr(stream)), self.h)
+        return logits[:n.value]
+
+    # ---- decode loops ---------------------------------------------------------------------
+    def generate_streaming(self, prompt, max_new_tokens: int, window_size: int,
+                           params: SamplingParams, seq: int = 0, stream=None):
+        """``WeDLMDecoder::generate_streaming``: returns (prompt + generated ids, stats)."""
+        import numpy as np
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(max(max_new_tokens, 1), np.int32)
+        n = C.c_int32()
+        st = WedlmBlockStats()
+        pc = params.to_c()
+        check(lib().wedlm_generate_streaming(self.h, seq, p.ctypes.data, p.size, max_new_tokens,
+                                             window_size, C.byref(pc), out.ctypes.data,
+                                             C.byref(n), C.byref(st), stream_ptr(stream)), self.h)
+        stats = {f: getattr(st, f) for f, _ in WedlmBlockStats._fields_}
+        return list(p) + out[:n.value].tolist(), stats
+
+    def generate_streaming_batch(self, prompts, max_new_tokens: int, window_size: int,
+                                 params: SamplingParams, stream=None):
+        import numpy as np
+        p = np.ascontiguousarray(prompts, dtype=np.int32)
+        nseq, P = p.shape
+        out = np.zeros((nseq, max(max_new_tokens, 1)), np.int32)
+        n = np.zeros(nseq, np.int32)
+        steps = np.zeros(nseq, np.int64)
+        pc = params.to_c()
+        check(lib().wedlm_generate_streaming_batch(self.h, nseq, p.ctypes.data, P, max_new_tokens,
+                                                   window_size, C.byref(pc), out.ctypes.data,
+                                                   n.ctypes.data, steps.ctypes.data,
+                                                   stream_ptr(stream)), self.h)
+        return [out[b, :n[b]].tolist() for b in range(nseq)], steps
