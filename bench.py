@@ -11,7 +11,14 @@ Workloads (seeded synthetic inputs; no dataset is involved):
   N(8, 1) spike per row; tau 0.8, lambda 0.05, cap 8, T 0.  A step is one
   ``wedlm_entropy_select`` over the whole batch.  Multi-GPU: every rank runs its own
   batch (weak scaling, no collective on the data path).
-* ``decode_8b`` -- streaming block decode of the 8B-shape random-init bf16 model.
+* ``decode_8b`` (default) -- streaming block decode of the 8B-shape random-init bf16
+  model (36 layers, hidden 4096, 32/8 heads, head_dim 128, SwiGLU 12288, vocab 151936,
+  N(0, 0.02^2) weights, norm weights 1): a 512-token uniform random prompt, then 512
+  tokens generated with window 96 and the balanced preset (tau 0.8, lambda 0.05, cap 8
+  with the entropy-EMA rule), temperature 0.  A step is one iteration of the streaming
+  loop: one forward of the 96-token window against the KV cache, the fused
+  entropy-select pass and the commit.  Multi-GPU: one independent sequence per rank
+  (data-parallel replicas, weak scaling, no collective on the data path).
 
 For N > 1 launch with ``torchrun --nproc-per-node N bench.py --gpus N``.
 """
@@ -320,13 +327,252 @@ def reference_entropy(args, rank, ws):
 
 
 # ----------------------------------------------------------------------------------
+PROMPT_8B, NEW_8B, WINDOW_8B = 512, 512, 96
+
+
+def balanced_params():
+    from wedlm_b200 import SamplingParams
+    return SamplingParams.preset("balanced", temperature=0.0)
+
+
+def make_prompt(n: int, seed: int, vocab_hi: int = 151643):
+    import numpy as np
+    # uniform ids below the special-token range (eos 151643, mask 151665)
+    return np.random.default_rng(seed).integers(0, vocab_hi, size=n).astype(np.int32)
+
+
+def bench_decode_8b(args, rank, ws, local):
+    import torch
+    from wedlm_b200 import Context, ModelConfig
+    hbm, tflops, peak_kind = peaks()
+    cfg = ModelConfig.wedlm_8b(max_block_tokens=WINDOW_8B)
+    max_ctx = PROMPT_8B + NEW_8B + WINDOW_8B + 64
+    ctx = Context(cfg, device=local, max_seqs=1, max_ctx=max_ctx)
+    ctx.init_random(seed=0, std=0.02)
+    prompt = make_prompt(PROMPT_8B, seed=rank)
+    params = balanced_params()
+    stream = torch.cuda.current_stream()
+    # warm the kernels, tensor maps and scratch on a short run
+    ctx.generate_streaming(prompt[:64], 8, WINDOW_8B, params)
+    torch.cuda.synchronize()
+
+    need = args.warmup + args.steps + args.profile_steps
+    assert need < NEW_8B, "steps exceed one 512-token generation"
+    ctx.decode_begin([0], prompt, NEW_8B, WINDOW_8B, params)
+    ctx.decode_step(args.warmup)
+    _, st0 = ctx.decode_result(0)
+    n0, h0, d0 = ctx.decode_io_bytes()
+    launches0 = ctx.launch_count()
+    clk = ClockSampler(local)
+    clk.start()
+    time.sleep(0.3)
+    barrier(ws)
+    torch.cuda.synchronize()
+    t0 = time.time()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        ctx.decode_step(1)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier(ws)
+    t1 = time.time()
+    clocks = clk.stop(t0, t1)
+    ms = ev0.elapsed_time(ev1) / args.steps
+    _, st1 = ctx.decode_result(0)
+    n1, h1, d1 = ctx.decode_io_bytes()
+    launches = ctx.launch_count() - launches0
+    toks = st1["tokens_generated"] - st0["tokens_generated"]
+    ms_max = max_over_ranks(ms, ws)
+    tok_total = toks
+    if ws > 1:
+        import torch.distributed as dist
+        t = torch.tensor([float(toks)], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t)
+        tok_total = float(t.item())
+    value = tok_total / (ms_max * args.steps * 1e-3)
+
+    # per-kernel-class device time over a further measured region
+    ctx.profile_enable(True)
+    ctx.decode_step(args.profile_steps)
+    prof = ctx.profile_read()
+    ctx.profile_enable(False)
+    ctx.decode_end()
+
+    # end to end through the public generate call: prompt from host, ids back to host
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(ws)
+    e0.record(stream)
+    ids, est = ctx.generate_streaming(prompt, NEW_8B, WINDOW_8B, params)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_s = max_over_ranks(e0.elapsed_time(e1) / 1e3, ws)
+    e2e_tok = est["tokens_generated"] * ws
+    steps_timed = max(n1 - n0, 1)
+
+    g = prof["gemm"]
+    gemm_gbs = g["bytes"] / (g["ms"] * 1e-3) / 1e9 if g["ms"] > 0 else None
+    a = prof["attention"]
+    e = prof["entropy"]
+    step_ms_prof = sum(v["ms"] for v in prof.values()) / max(args.profile_steps, 1)
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "committed tok/s",
+        "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_max, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: random-init N(0,0.02^2) 8B-shape weights, uniform random prompt ids",
+        "config": {"workload": "decode_8b: 8B-shape WeDLM, 512-token prompt, 512 new tokens, "
+                               "window 96, balanced preset (tau 0.8, lambda 0.05, cap 8), T 0",
+                   "layers": 36, "hidden": 4096, "heads": "32/8", "head_dim": 128,
+                   "ffn": 12288, "vocab": 151936, "window": WINDOW_8B,
+                   "tokens_per_step": round(toks / args.steps, 3),
+                   "l2": "inputs larger than L2 (15.1 GB of weights streamed per step)",
+                   "parallelism": f"dp{ws} (one independent sequence per GPU)"},
+        "clocks": clocks,
+        "e2e": {"value": round(e2e_tok / e2e_s, 2), "unit": "committed tok/s",
+                "h2d_bytes_per_step": int((h1 - h0) / steps_timed),
+                "d2h_bytes_per_step": int((d1 - d0) / steps_timed),
+                "scope": "wedlm_generate_streaming: 512-token prompt prefill + 512 tokens, "
+                         "host ids in and out"},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "hbm", "achieved": round(gemm_gbs, 1) if gemm_gbs else None,
+                     "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s",
+                     "frac": round(gemm_gbs / hbm, 4) if gemm_gbs else None,
+                     "traffic": profile_traffic("gemm_tc_decode_8b.md"),
+                     "kernel": "gemm_tc_kernel (+ shared-tile reduce): QKV/O/gate-up/down/LM head",
+                     "launches_per_step": round(g["launches"] / max(args.profile_steps, 1), 1),
+                     "share_of_step": round(g["ms"] / max(sum(v["ms"] for v in prof.values()), 1e-9), 3)},
+        "kernel_classes": {k: {"ms_per_step": round(v["ms"] / max(args.profile_steps, 1), 4),
+                               "GBps": round(v["bytes"] / (v["ms"] * 1e-3) / 1e9, 1) if v["ms"] > 0 else None,
+                               "TFLOPs": round(v["flops"] / (v["ms"] * 1e-3) / 1e12, 1) if v["ms"] > 0 and v["flops"] > 0 else None,
+                               "launches_per_step": round(v["launches"] / max(args.profile_steps, 1), 1)}
+                           for k, v in prof.items()},
+        "profiled_step_ms": round(step_ms_prof, 3),
+    }
+    ctx.close()
+    del ctx
+    torch.cuda.empty_cache()
+    if not args.no_entropy:
+        args2 = argparse.Namespace(**vars(args))
+        args2.profile, args2.no_cpu_baseline, args2.hold_seconds = False, True, 0.5
+        es = bench_entropy_select(args2, rank, ws, local)
+        line["entropy_select"] = {
+            "workload": es["config"]["workload"], "value": es["value"], "unit": "GB/s",
+            "ms_per_step": es["ms_per_step"], "roofline": es["roofline"], "e2e": es["e2e"],
+            "clocks": es["clocks"]}
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_decode(args.cpu_seconds)
+    return line
+
+
+class OracleDecodeSample:
+    """A bounded sample of the decode step on the host cores, following the oracle: one
+    of the 36 8B-shape layers over a 96-row window against a 1024-token cache, the LM
+    head over the 96 rows for 1/8 of the vocabulary, and the C restatement of the
+    entropy / selection / argmax stage over 96 x 151936 logits.  ``run()`` returns the
+    extrapolated seconds of one full step (36 layers, whole vocabulary)."""
+
+    def __init__(self, seed: int = 0):
+        import numpy as np
+        from oracle.model import (OracleModel, WeDLMConfig, f32_to_bf16_bits, rope_tables,
+                                  weight_names)
+        cfg = WeDLMConfig.wedlm_8b()
+        one = WeDLMConfig(**{**cfg.to_dict(), "num_hidden_layers": 1,
+                             "vocab_size": 151936 // 8, "dtype": "float32"})
+        rng = np.random.default_rng(seed)
+        H = one.hidden_size
+        w = {}
+        for name, shape in weight_names(one):
+            if name.endswith("norm.weight"):
+                w[name] = np.ones(shape, np.float32)
+            elif name == "model.embed_tokens.weight":
+                w[name] = np.zeros((8, H), np.float32)
+            else:
+                w[name] = rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)
+        m = OracleModel.__new__(OracleModel)
+        m.cfg, m.dtype, m._r, m.w = one, "f32", (lambda a: np.asarray(a, np.float32)), w
+        m.cos, m.sin = rope_tables(one.head_dim, 2048, one.rope_theta, False)
+        self.m, self.w = m, w
+        L, S = 1024, 96
+        self.S = S
+        self.cache = (rng.standard_normal((8, L, 128), dtype=np.float32),
+                      rng.standard_normal((8, L, 128), dtype=np.float32))
+        self.h = rng.standard_normal((S, H), dtype=np.float32)
+        self.pos = L + rng.permutation(S)
+        self.logits = f32_to_bf16_bits(rng.standard_normal((S, 151936), dtype=np.float32) * 2.5)
+        self.desc = ""
+
+    def run(self) -> float:
+        import numpy as np
+        from oracle import cbind
+        S = self.S
+        t0 = time.time()
+        h2, _ = self.m._layer(0, self.h, self.pos, self.cache, np.arange(S))
+        t_layer = time.time() - t0
+        t0 = time.time()
+        np.matmul(h2, self.w["lm_head.weight"].T)
+        t_head = (time.time() - t0) * 8
+        t0 = time.time()
+        cbind.entropy_select(self.logits, "bf16", 0.0, 0.8, 0.05, [0, S], list(range(S)), [8])
+        t_ent = time.time() - t0
+        self.desc = (f"1 of 36 layers ({t_layer:.3f} s) x 36 + LM head on 1/8 of the vocabulary "
+                     f"({t_head / 8:.3f} s) x 8 + entropy/selection over 96 x 151936 "
+                     f"({t_ent:.3f} s); numpy f32 with BLAS threads and the C restatement")
+        return 36 * t_layer + t_head + t_ent
+
+
+def cpu_baseline_decode(budget_s: float):
+    import os as _os
+    smp = OracleDecodeSample()
+    smp.run()
+    steps, t0 = [], time.time()
+    while True:
+        steps.append(smp.run())
+        if time.time() - t0 >= budget_s:
+            break
+    step = sum(steps) / len(steps)
+    return {"value": round(1.0 / step, 4), "unit": "committed tok/s", "cores": _os.cpu_count(),
+            "kind": "port",
+            "sample": smp.desc + f"; {len(steps)} samples, extrapolated {step:.2f} s per step, "
+                                 "1 committed token per step (random-init entropy >> tau)"}
+
+
+def reference_decode(args, rank, ws):
+    """--impl reference for decode_8b: the reference's algorithm on the host cores (the
+    oracle port; the Rust crate cannot be built without cargo and candle), each step a
+    bounded sample extrapolated to a full 36-layer step."""
+    import os as _os
+    smp = OracleDecodeSample()
+    for _ in range(args.warmup):
+        smp.run()
+    steps = [smp.run() for _ in range(args.steps)]
+    desc = smp.desc
+    step = sum(steps) / len(steps)
+    v = 1.0 / step
+    return {"metric": METRIC, "value": round(v, 4), "unit": "committed tok/s",
+            "impl": "reference", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(step * 1e3, 1), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "decode_8b: 8B-shape WeDLM, window 96, balanced preset, T 0 "
+                                   "(one step = one window forward + entropy-select + commit)"},
+            "cpu_baseline": {"value": round(v, 4), "unit": "committed tok/s",
+                             "cores": _os.cpu_count(), "kind": "port", "sample": desc},
+            "e2e": {"value": round(v, 4), "unit": "committed tok/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+# ----------------------------------------------------------------------------------
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="entropy_select", choices=["entropy_select"])
+    ap.add_argument("--workload", default="decode_8b", choices=["decode_8b", "entropy_select"])
+    ap.add_argument("--profile-steps", type=int, default=10,
+                    help="decode steps timed per kernel class after the headline region")
+    ap.add_argument("--no-entropy", action="store_true",
+                    help="skip the entropy-select sub-measurement of decode_8b")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--nseq", type=int, default=64, help="sequences of 96 mask rows per GPU")
@@ -343,11 +589,15 @@ def main():
         ws = int(os.environ.get("WORLD_SIZE", "1"))
         if rank != 0:
             return
-        print(json.dumps(reference_entropy(args, rank, ws)), flush=True)
+        fn = reference_decode if args.workload == "decode_8b" else reference_entropy
+        print(json.dumps(fn(args, rank, ws)), flush=True)
         return
 
     rank, ws, local = dist_setup(args.gpus)
-    line = bench_entropy_select(args, rank, ws, local)
+    if args.workload == "decode_8b":
+        line = bench_decode_8b(args, rank, ws, local)
+    else:
+        line = bench_entropy_select(args, rank, ws, local)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if ws > 1:

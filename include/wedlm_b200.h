@@ -198,6 +198,26 @@ WEDLM_API int wedlm_generate_streaming(wedlm_ctx* ctx, int seq, const int32_t* p
                              const wedlm_sampling_params* params, int32_t* out_ids,
                              int32_t* n_out, wedlm_block_stats* stats, void* stream);
 
+/* Step-wise form of the streaming decode for nseq independent sequences (cache slots
+ * seq_ids, prompts host [nseq, n_prompt]), stepped together with one forward per step
+ * over all live windows.  wedlm_decode_begin prefills the prompts and sets up the
+ * windows; wedlm_decode_step runs up to n_steps iterations of the loop body of
+ * WeDLMDecoder::generate_streaming (src/decoding/wedlm.rs:380-573), synchronising
+ * `stream` once per step, and reports how many sequences are still generating;
+ * wedlm_decode_result copies sequence b's generated ids (host, up to max_new_tokens)
+ * and stats; wedlm_decode_end releases the session.  One session per context. */
+WEDLM_API int wedlm_decode_begin(wedlm_ctx* ctx, int nseq, const int32_t* seq_ids,
+                                 const int32_t* prompts, int n_prompt, int max_new_tokens,
+                                 int window_size, const wedlm_sampling_params* params,
+                                 void* stream);
+WEDLM_API int wedlm_decode_step(wedlm_ctx* ctx, int n_steps, int32_t* n_live);
+WEDLM_API int wedlm_decode_result(wedlm_ctx* ctx, int b, int32_t* out_ids, int32_t* n_out,
+                                  wedlm_block_stats* stats);
+/* Steps run so far and the host<->device bytes they moved (inputs up, results down). */
+WEDLM_API int wedlm_decode_io_bytes(const wedlm_ctx* ctx, int64_t* steps, int64_t* h2d_bytes,
+                                    int64_t* d2h_bytes);
+WEDLM_API int wedlm_decode_end(wedlm_ctx* ctx);
+
 /* Batched streaming decode: nseq independent sequences stepped together, one
  * forward per step over all live windows (data-parallel batching of
  * generate_streaming).  prompts: host [nseq, n_prompt]; out_ids: host

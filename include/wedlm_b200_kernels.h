@@ -35,6 +35,25 @@ WEDLM_API int wedlm_kernel_gemm(wedlm_ctx* ctx, const void* X, int64_t ldx, cons
  * inside a kernel since the last check: WEDLM_ERR_TIMEOUT, else WEDLM_OK. */
 WEDLM_API int wedlm_check_device_error(wedlm_ctx* ctx, void* stream);
 
+/* Kernel classes of the profiler. */
+enum wedlm_kernel_class {
+  WEDLM_KC_GEMM = 0,       /* projection GEMMs (tcgen05) incl. their shared-tile reduce */
+  WEDLM_KC_ATTENTION = 1,  /* block attention incl. the split-KV combine               */
+  WEDLM_KC_ENTROPY = 2,    /* fused entropy-select                                      */
+  WEDLM_KC_OTHER = 3       /* embedding, RMSNorm, RoPE/KV append, row gather            */
+};
+
+/* Time every launch of the model forward and the entropy stage with CUDA events on the
+ * launching stream, per kernel class (on = 1 clears the totals).  Events sit between
+ * launches, so keep it off for headline timings. */
+WEDLM_API int wedlm_profile_enable(wedlm_ctx* ctx, int on);
+/* Totals of class `cls` since profiling was enabled: device milliseconds, algorithmic
+ * bytes and flops (the minimum a launch must move / compute), number of kernels. */
+WEDLM_API int wedlm_profile_read(wedlm_ctx* ctx, int cls, double* ms, double* bytes,
+                                 double* flops, int64_t* launches);
+/* Kernels this context has launched for forwards and entropy passes so far. */
+WEDLM_API int wedlm_launch_count(const wedlm_ctx* ctx, int64_t* out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -230,3 +230,20 @@ def test_wide_bf16_prefill_chunks_equal_one_forward(wide):
     ref, _ = om.forward_with_positions(ids[280:], np.arange(280, 300), cache, round_logits=False)
     err = np.abs(tail - ref)
     assert err.mean() <= 0.015 and err.max() <= 0.1, (err.mean(), err.max())
+
+
+def test_c1_decode_session_step_by_step(c1):
+    """wedlm_decode_begin / step / result equal one generate_streaming call."""
+    cfg, w, ctx, om = c1
+    prompt = np.random.default_rng(9).integers(1, 4095, size=24).tolist()
+    ctx.decode_begin([2], [prompt], 30, 12, params(9.0, 0.01, 3))
+    live, n = 1, 0
+    while live:
+        live = ctx.decode_step(1)
+        n += 1
+    ids, st = ctx.decode_result(0)
+    steps, h2d, d2h = ctx.decode_io_bytes()
+    ctx.decode_end()
+    ref, rst = ctx.generate_streaming(prompt, 30, 12, params(9.0, 0.01, 3), seq=2)
+    assert prompt + ids == ref and st["steps"] == rst["steps"] == steps
+    assert h2d > 0 and d2h > 0

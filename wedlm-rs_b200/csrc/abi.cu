@@ -101,6 +101,44 @@ Status check_device_error(wedlm_ctx* ctx, cudaStream_t st) {
   return Status::ok();
 }
 
+int prof_begin(wedlm_ctx* ctx, cudaStream_t st) {
+  WedlmProfiler& P = ctx->prof;
+  if (!P.on) return -1;
+  if (P.next + 2 > (int)P.ev.size()) {
+    const int n = (int)P.ev.size();
+    P.ev.resize(n + 2048);
+    for (int i = n; i < (int)P.ev.size(); ++i) cudaEventCreate(&P.ev[i]);
+  }
+  const int h = P.next;
+  P.next += 2;
+  cudaEventRecord(P.ev[h], st);
+  return h;
+}
+
+void prof_end(wedlm_ctx* ctx, cudaStream_t st, int h, int cls, double bytes, double flops,
+              int nlaunch) {
+  WedlmProfiler& P = ctx->prof;
+  ctx->launches += nlaunch;
+  if (!P.on || h < 0) return;
+  cudaEventRecord(P.ev[h + 1], st);
+  P.pending.push_back(WedlmProfiler::Rec{cls, h, h + 1, bytes, flops});
+  P.launches[cls] += nlaunch;
+}
+
+void prof_collect(wedlm_ctx* ctx) {
+  WedlmProfiler& P = ctx->prof;
+  for (const auto& r : P.pending) {
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, P.ev[r.e0], P.ev[r.e1]) == cudaSuccess) {
+      P.ms[r.cls] += ms;
+      P.bytes[r.cls] += r.bytes;
+      P.flops[r.cls] += r.flops;
+    }
+  }
+  P.pending.clear();
+  P.next = 0;
+}
+
 }  // namespace wedlm
 
 extern "C" {
@@ -151,6 +189,8 @@ void wedlm_destroy(wedlm_ctx* ctx) {
   if (!ctx) return;
   cudaSetDevice(ctx->device);
   cudaDeviceSynchronize();
+  wedlm::session_free(ctx);
+  for (cudaEvent_t e : ctx->prof.ev) cudaEventDestroy(e);
   wedlm::model_destroy(ctx);
   wedlm::free_entropy_scratch(ctx);
   wedlm::free_gemm_scratch(ctx);
@@ -283,4 +323,40 @@ extern "C" int wedlm_check_device_error(wedlm_ctx* ctx, void* stream) {
   if (int rc = set_device(ctx)) return rc;
   wedlm::Status s = wedlm::check_device_error(ctx, (cudaStream_t)stream);
   return s.good() ? WEDLM_OK : ctx->fail(s);
+}
+
+extern "C" int wedlm_profile_enable(wedlm_ctx* ctx, int on) {
+  if (!ctx) return WEDLM_ERR_INVALID_ARG;
+  if (int rc = set_device(ctx)) return rc;
+  cudaDeviceSynchronize();
+  wedlm::prof_collect(ctx);
+  WedlmProfiler& P = ctx->prof;
+  if (on && !P.on) {
+    for (int c = 0; c < WedlmProfiler::kClasses; ++c) {
+      P.ms[c] = P.bytes[c] = P.flops[c] = 0;
+      P.launches[c] = 0;
+    }
+  }
+  P.on = on != 0;
+  return WEDLM_OK;
+}
+
+extern "C" int wedlm_profile_read(wedlm_ctx* ctx, int cls, double* ms, double* bytes,
+                                  double* flops, int64_t* launches) {
+  if (!ctx || cls < 0 || cls >= WedlmProfiler::kClasses) return WEDLM_ERR_INVALID_ARG;
+  if (int rc = set_device(ctx)) return rc;
+  cudaDeviceSynchronize();
+  wedlm::prof_collect(ctx);
+  const WedlmProfiler& P = ctx->prof;
+  if (ms) *ms = P.ms[cls];
+  if (bytes) *bytes = P.bytes[cls];
+  if (flops) *flops = P.flops[cls];
+  if (launches) *launches = P.launches[cls];
+  return WEDLM_OK;
+}
+
+extern "C" int wedlm_launch_count(const wedlm_ctx* ctx, int64_t* out) {
+  if (!ctx || !out) return WEDLM_ERR_INVALID_ARG;
+  *out = ctx->launches;
+  return WEDLM_OK;
 }

@@ -11,7 +11,24 @@
 
 namespace wedlm {
 struct ModelState;
+struct DecodeSession;
 }
+
+// Optional per-kernel-class timing with CUDA events on the launching stream
+// (enabled around a measured region; the events are recorded between launches).
+struct WedlmProfiler {
+  enum { kGemm = 0, kAttention = 1, kEntropy = 2, kOther = 3, kClasses = 4 };
+  bool on = false;
+  std::vector<cudaEvent_t> ev;
+  struct Rec {
+    int cls, e0, e1;
+    double bytes, flops;
+  };
+  std::vector<Rec> pending;
+  int next = 0;
+  double ms[kClasses] = {}, bytes[kClasses] = {}, flops[kClasses] = {};
+  int64_t launches[kClasses] = {};
+};
 
 struct wedlm_ctx {
   int device = 0;
@@ -31,8 +48,14 @@ struct wedlm_ctx {
   int gemm_n_counters = 0;
   int* dev_err = nullptr;
 
+  // kernels launched by this context (always counted) and the optional profiler
+  int64_t launches = 0;
+  WedlmProfiler prof;
+
   // model state (model.cu); opaque here
   wedlm::ModelState* model = nullptr;
+  // step-wise streaming decode (decode.cu); at most one per context
+  wedlm::DecodeSession* session = nullptr;
 
   int fail(const wedlm::Status& s) {
     last_error = s.msg;
@@ -51,5 +74,14 @@ Status ensure_gemm_scratch(wedlm_ctx* ctx, long ws_floats, int counters);
 void free_gemm_scratch(wedlm_ctx* ctx);
 // Read and clear the device error word; a non-zero code means a bounded wait gave up.
 Status check_device_error(wedlm_ctx* ctx, cudaStream_t st);
+void session_free(wedlm_ctx* ctx);
+// Profiler: mark the start of a launch group; returns a handle (or -1 when off).
+int prof_begin(wedlm_ctx* ctx, cudaStream_t st);
+// End the group started by prof_begin: `nlaunch` kernels of class `cls` that moved
+// `bytes` algorithmic bytes and did `flops` algorithmic flops.
+void prof_end(wedlm_ctx* ctx, cudaStream_t st, int h, int cls, double bytes, double flops,
+              int nlaunch);
+// Fold completed event pairs into the totals (call after the stream synchronised).
+void prof_collect(wedlm_ctx* ctx);
 
 }  // namespace wedlm

@@ -198,7 +198,7 @@ __device__ void finalize_sequence(int b, int r0, int r1, const float* part, long
                                   int nk, float tau, float lambda, const int* __restrict__ mask_pos,
                                   const int* __restrict__ caps, float* row_H, float* H,
                                   int* argmax, float* maxprob, int* selected, int* n_selected,
-                                  float* running) {
+                                  float* running, const int* running_idx) {
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
   const int M = r1 - r0;
   for (int r = r0 + w; r < r1; r += kThreads / 32) {
@@ -247,8 +247,9 @@ __device__ void finalize_sequence(int b, int r0, int r1, const float* part, long
       for (int i = 0; i < M; ++i) sum = __fadd_rn(sum, __ldcg(row_H + r0 + i));
       const float mean = __fdiv_rn(sum, (float)M);
       const float a = 0.3f;
-      const float r = __fadd_rn(__fmul_rn(a, mean), __fmul_rn(__fsub_rn(1.f, a), running[b]));
-      running[b] = r;
+      const int ri = running_idx ? running_idx[b] : b;
+      const float r = __fadd_rn(__fmul_rn(a, mean), __fmul_rn(__fsub_rn(1.f, a), running[ri]));
+      running[ri] = r;
       if (r < __fmul_rn(tau, 0.4f)) cap0 = cap0 * 2;
       else if (r < __fmul_rn(tau, 0.7f)) cap0 = (cap0 * 3 + 1) / 2;
     }
@@ -344,7 +345,7 @@ entropy_select_kernel(const T* __restrict__ logits, int V, long ld, int splits, 
                       int nseq, const int* __restrict__ seq_rows, const int* __restrict__ mask_pos,
                       const int* __restrict__ caps, float tau, float lambda,
                       float* __restrict__ row_H, float* H, int* argmax, float* maxprob,
-                      int* selected, int* n_selected, float* running) {
+                      int* selected, int* n_selected, float* running, const int* running_idx) {
   const int row = blockIdx.x / splits;
   const int split = blockIdx.x - row * splits;
   const int c0 = split * split_cols;
@@ -379,7 +380,8 @@ entropy_select_kernel(const T* __restrict__ logits, int V, long ld, int splits, 
   __threadfence();
   const int b = s_seq;
   finalize_sequence(b, seq_rows[b], seq_rows[b + 1], part, splits, 1, splits, tau, lambda,
-                    mask_pos, caps, row_H, H, argmax, maxprob, selected, n_selected, running);
+                    mask_pos, caps, row_H, H, argmax, maxprob, selected, n_selected, running,
+                    running_idx);
   if (threadIdx.x == 0) seq_count[b] = 0u;
 }
 
@@ -424,10 +426,11 @@ __global__ void __launch_bounds__(kThreads)
 entropy_combine_kernel(const float* __restrict__ part, int nshards, int rows, const int* seq_rows,
                        const int* mask_pos, const int* caps, float tau, float lambda,
                        float* row_H, float* H, int* argmax, float* maxprob, int* selected,
-                       int* n_selected, float* running) {
+                       int* n_selected, float* running, const int* running_idx) {
   const int b = blockIdx.x;
   finalize_sequence(b, seq_rows[b], seq_rows[b + 1], part, 1, rows, nshards, tau, lambda,
-                    mask_pos, caps, row_H, H, argmax, maxprob, selected, n_selected, running);
+                    mask_pos, caps, row_H, H, argmax, maxprob, selected, n_selected, running,
+                    running_idx);
 }
 
 int pick_splits(int rows, int V, int num_sms) {
@@ -448,12 +451,12 @@ void launch_select(const EntropyArgs& A, const EntropyScratch& W, int splits, in
     entropy_select_kernel<T, true><<<grid, kThreads, 0, st>>>(
         (const T*)A.logits, A.V, A.ld, splits, split_cols, invT, W.partials, W.seq_count, A.nseq,
         A.seq_rows, A.mask_pos, A.caps, A.tau, A.lambda, W.row_H, A.H, A.argmax, A.maxprob,
-        A.selected, A.n_selected, A.running);
+        A.selected, A.n_selected, A.running, A.running_idx);
   else
     entropy_select_kernel<T, false><<<grid, kThreads, 0, st>>>(
         (const T*)A.logits, A.V, A.ld, splits, split_cols, invT, W.partials, W.seq_count, A.nseq,
         A.seq_rows, A.mask_pos, A.caps, A.tau, A.lambda, W.row_H, A.H, A.argmax, A.maxprob,
-        A.selected, A.n_selected, A.running);
+        A.selected, A.n_selected, A.running, A.running_idx);
 }
 
 template <typename T>
@@ -542,7 +545,7 @@ Status run_entropy_combine(const float* partials, int nshards, const EntropyArgs
   entropy_combine_kernel<<<A.nseq, kThreads, 0, st>>>(partials, nshards, A.rows, A.seq_rows,
                                                       A.mask_pos, A.caps, A.tau, A.lambda, W.row_H,
                                                       A.H, A.argmax, A.maxprob, A.selected,
-                                                      A.n_selected, A.running);
+                                                      A.n_selected, A.running, A.running_idx);
   WEDLM_CUDA_TRY(cudaGetLastError());
   return Status::ok();
 }

@@ -18,7 +18,8 @@ struct EntropyArgs {
   // Optional streaming-decode mode (wedlm.rs:517-535): when `running` is set, each
   // sequence's entropy EMA running[b] is updated with the mean entropy of its rows and
   // the cap becomes the dynamic cap derived from caps[b] (the preset cap).
-  float* running = nullptr;       // device [nseq]
+  float* running = nullptr;       // device, indexed by running_idx[b] (or b)
+  const int* running_idx = nullptr;
   float* H = nullptr;
   int* argmax = nullptr;
   float* maxprob = nullptr;

@@ -473,7 +473,12 @@ Status model_forward(wedlm_ctx* ctx, const std::vector<SeqSlice>& seqs, const in
   if (!ctx->dev_err) WEDLM_TRY(ensure_gemm_scratch(ctx, 0, 0));
   int* err = ctx->dev_err;
 
-  WEDLM_TRY(run_embed(m->embed, m->dt, d + o_tok, R, m->H, m->V, m->h, err, st));
+  {
+    const int ph = prof_begin(ctx, st);
+    Status se = run_embed(m->embed, m->dt, d + o_tok, R, m->H, m->V, m->h, err, st);
+    prof_end(ctx, st, ph, WedlmProfiler::kOther, 2.0 * R * m->H * es, 0, 1);
+    WEDLM_TRY(se);
+  }
 
   // attention geometry shared by the layers
   AttnArgs aa;
@@ -551,27 +556,57 @@ Status model_forward(wedlm_ctx* ctx, const std::vector<SeqSlice>& seqs, const in
     g.ldo = ldo;
     g.resid = resid;
     g.ldr = ldr;
-    if (!tc) return run_gemm_f32(g, st);
+    const double nw = W2 ? 2.0 : 1.0;
+    const double bytes = nw * N * K * es + (double)M * K * es +
+                         (double)M * N * (epi == EPI_STORE_F32 ? 4 : es) * (epi == EPI_RESID_BF16 ? 2 : 1);
+    const double flops = 2.0 * nw * M * N * K;
+    if (!tc) {
+      const int ph = prof_begin(ctx, st);
+      Status s = run_gemm_f32(g, st);
+      prof_end(ctx, st, ph, WedlmProfiler::kGemm, bytes, flops, 1);
+      return s;
+    }
     GemmPlan gp = plan_gemm_tc(M, N, K, epi == EPI_SWIGLU_BF16, ctx->num_sms);
     WEDLM_TRY(ensure_gemm_scratch(ctx, gp.ws_floats, gp.counters));
-    return run_gemm_tc(g, gp, ctx->gemm_ws, ctx->gemm_counters, ctx->dev_err, st);
+    const int ph = prof_begin(ctx, st);
+    Status s = run_gemm_tc(g, gp, ctx->gemm_ws, ctx->gemm_counters, ctx->dev_err, st);
+    prof_end(ctx, st, ph, WedlmProfiler::kGemm, bytes, flops, gp.grid > 1 ? 2 : 1);
+    return s;
+  };
+  // algorithmic bytes / flops of the other kernels of one layer
+  double attn_bytes = 2.0 * R * m->qdim * es, attn_flops = 0;
+  for (int b = 0; b < B; ++b) {
+    attn_bytes += 2.0 * (h_len[b] + h_rows[b]) * m->kvdim * es;
+    attn_flops += 4.0 * m->nh * m->d * h_rows[b] * (h_len[b] + (h_rows[b] + 1) / 2.0);
+  }
+  const double norm_bytes = 2.0 * R * m->H * es;
+  const double rope_bytes = (double)R * m->qkvdim * es * 2;
+  auto other = [&](Status s, int ph, double bytes) {
+    prof_end(ctx, st, ph, WedlmProfiler::kOther, bytes, 0, 1);
+    return s;
   };
 
   for (int l = 0; l < m->nlayers; ++l) {
     const LayerWeights& L = m->layers[l];
-    WEDLM_TRY(run_rmsnorm(m->h, H, L.ln1, R, m->H, m->eps, m->dt, m->xn, H, st));
+    int ph = prof_begin(ctx, st);
+    WEDLM_TRY(other(run_rmsnorm(m->h, H, L.ln1, R, m->H, m->eps, m->dt, m->xn, H, st), ph, norm_bytes));
     WEDLM_TRY(gemm(m->xn, H, L.wqkv, nullptr, m->qkvdim, m->H, EPI_STORE_BF16, m->qkv, m->qkvdim,
                    nullptr, 0, R));
     rk.layer = l;
     rk.q_norm = L.qn;
     rk.k_norm = L.kn;
-    WEDLM_TRY(run_rope_kv(rk, m->dt, st));
+    ph = prof_begin(ctx, st);
+    WEDLM_TRY(other(run_rope_kv(rk, m->dt, st), ph, rope_bytes));
     aa.layer = l;
+    ph = prof_begin(ctx, st);
     if (tc) WEDLM_TRY(run_attention_tc(aa, plan, err, st));
     else WEDLM_TRY(run_attention_f32(aa, st));
+    prof_end(ctx, st, ph, WedlmProfiler::kAttention, attn_bytes, attn_flops,
+             tc ? 1 + (plan.n_comb > 0) : 1);
     WEDLM_TRY(gemm(m->attn, m->qdim, L.wo, nullptr, m->H, m->qdim, EPI_RESID_BF16, m->h, H, m->h,
                    H, R));
-    WEDLM_TRY(run_rmsnorm(m->h, H, L.ln2, R, m->H, m->eps, m->dt, m->xn, H, st));
+    ph = prof_begin(ctx, st);
+    WEDLM_TRY(other(run_rmsnorm(m->h, H, L.ln2, R, m->H, m->eps, m->dt, m->xn, H, st), ph, norm_bytes));
     WEDLM_TRY(gemm(m->xn, H, L.wgate, L.wup, m->I, m->H, EPI_SWIGLU_BF16, m->act, m->I, nullptr, 0,
                    R));
     WEDLM_TRY(gemm(m->act, m->I, L.wdown, nullptr, m->H, m->I, EPI_RESID_BF16, m->h, H, m->h, H, R));
@@ -579,9 +614,15 @@ Status model_forward(wedlm_ctx* ctx, const std::vector<SeqSlice>& seqs, const in
   for (int b = 0; b < B; ++b) m->pending_rows[seqs[b].slot] = seqs[b].rows;
   if (!logits || RL == 0) return Status::ok();
 
-  WEDLM_TRY(run_rmsnorm(m->h, H, m->final_norm, R, m->H, m->eps, m->dt, m->xn, H, st));
+  {
+    const int ph = prof_begin(ctx, st);
+    Status sn = run_rmsnorm(m->h, H, m->final_norm, R, m->H, m->eps, m->dt, m->xn, H, st);
+    prof_end(ctx, st, ph, WedlmProfiler::kOther, norm_bytes, 0, 1);
+    WEDLM_TRY(sn);
+  }
   const void* xl = m->xn;
   if (RL != R) {
+    ctx->launches += 1;
     if (m->dt == WEDLM_BF16)
       gather_rows_kernel<__nv_bfloat16><<<RL, 256, 0, st>>>(
           (const __nv_bfloat16*)m->xn, H, d + o_lsrc, (__nv_bfloat16*)m->xl, H, m->H);

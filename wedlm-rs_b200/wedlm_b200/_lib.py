@@ -77,10 +77,21 @@ _PROTOS = {
                                            C.POINTER(WedlmBlockStats), P]),
     "wedlm_generate_streaming_batch": (C.c_int, [P, C.c_int, P, C.c_int, C.c_int, C.c_int,
                                                  C.POINTER(WedlmSamplingParams), P, P, P, P]),
+    "wedlm_decode_begin": (C.c_int, [P, C.c_int, P, P, C.c_int, C.c_int, C.c_int,
+                                     C.POINTER(WedlmSamplingParams), P]),
+    "wedlm_decode_step": (C.c_int, [P, C.c_int, I32P]),
+    "wedlm_decode_result": (C.c_int, [P, C.c_int, P, I32P, C.POINTER(WedlmBlockStats)]),
+    "wedlm_decode_io_bytes": (C.c_int, [P, C.POINTER(C.c_int64), C.POINTER(C.c_int64),
+                                        C.POINTER(C.c_int64)]),
+    "wedlm_decode_end": (C.c_int, [P]),
     # kernel-level entry points (include/wedlm_b200_kernels.h)
     "wedlm_kernel_gemm": (C.c_int, [P, P, C.c_int64, P, P, C.c_int64, C.c_int, C.c_int, C.c_int,
                                     C.c_int, C.c_int, P, C.c_int64, P, C.c_int64, P]),
     "wedlm_check_device_error": (C.c_int, [P, P]),
+    "wedlm_profile_enable": (C.c_int, [P, C.c_int]),
+    "wedlm_profile_read": (C.c_int, [P, C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_double),
+                                     C.POINTER(C.c_double), C.POINTER(C.c_int64)]),
+    "wedlm_launch_count": (C.c_int, [P, C.POINTER(C.c_int64)]),
 }
 
 _lib = None

@@ -310,3 +310,58 @@ class Context:
                                                    n.ctypes.data, steps.ctypes.data,
                                                    stream_ptr(stream)), self.h)
         return [out[b, :n[b]].tolist() for b in range(nseq)], steps
+
+    # ---- step-wise streaming decode session ----------------------------------------------
+    def decode_begin(self, seq_ids, prompts, max_new_tokens: int, window_size: int,
+                     params: SamplingParams, stream=None) -> None:
+        import numpy as np
+        sid = np.ascontiguousarray(np.atleast_1d(seq_ids), dtype=np.int32)
+        p = np.ascontiguousarray(np.atleast_2d(prompts), dtype=np.int32)
+        self._decode_max_new = max_new_tokens
+        pc = params.to_c()
+        check(lib().wedlm_decode_begin(self.h, sid.size, sid.ctypes.data, p.ctypes.data,
+                                       p.shape[1], max_new_tokens, window_size, C.byref(pc),
+                                       stream_ptr(stream)), self.h)
+
+    def decode_step(self, n_steps: int = 1) -> int:
+        live = C.c_int32()
+        check(lib().wedlm_decode_step(self.h, n_steps, C.byref(live)), self.h)
+        return live.value
+
+    def decode_result(self, b: int = 0):
+        import numpy as np
+        out = np.zeros(max(self._decode_max_new, 1), np.int32)
+        n = C.c_int32()
+        st = WedlmBlockStats()
+        check(lib().wedlm_decode_result(self.h, b, out.ctypes.data, C.byref(n), C.byref(st)),
+              self.h)
+        return out[:n.value].tolist(), {f: getattr(st, f) for f, _ in WedlmBlockStats._fields_}
+
+    def decode_io_bytes(self):
+        s, a, b = C.c_int64(), C.c_int64(), C.c_int64()
+        check(lib().wedlm_decode_io_bytes(self.h, C.byref(s), C.byref(a), C.byref(b)), self.h)
+        return s.value, a.value, b.value
+
+    def decode_end(self) -> None:
+        check(lib().wedlm_decode_end(self.h), self.h)
+
+    # ---- profiling --------------------------------------------------------------------------
+    KERNEL_CLASSES = ("gemm", "attention", "entropy", "other")
+
+    def profile_enable(self, on: bool = True) -> None:
+        check(lib().wedlm_profile_enable(self.h, 1 if on else 0), self.h)
+
+    def profile_read(self) -> dict:
+        out = {}
+        for i, name in enumerate(self.KERNEL_CLASSES):
+            ms, by, fl, n = C.c_double(), C.c_double(), C.c_double(), C.c_int64()
+            check(lib().wedlm_profile_read(self.h, i, C.byref(ms), C.byref(by), C.byref(fl),
+                                           C.byref(n)), self.h)
+            out[name] = {"ms": ms.value, "bytes": by.value, "flops": fl.value,
+                         "launches": n.value}
+        return out
+
+    def launch_count(self) -> int:
+        v = C.c_int64()
+        check(lib().wedlm_launch_count(self.h, C.byref(v)), self.h)
+        return v.value
