@@ -327,6 +327,84 @@ def reference_entropy(args, rank, ws):
 
 
 # ----------------------------------------------------------------------------------
+# The projection GEMMs of one 8B decode step (M = 96 window rows), bf16, weights N x K.
+GEMM_SHAPES_8B = [("qkv", 6144, 4096, 0), ("o_resid", 4096, 4096, 2), ("gate_up_swiglu", 12288, 4096, 3),
+                  ("down_resid", 4096, 12288, 2), ("lm_head", 151936, 4096, 0)]
+
+
+def bench_gemm_shapes(args, rank, ws, local):
+    """The decode-step GEMM shapes on their own through wedlm_kernel_gemm: each step
+    runs every shape once; weights rotate over enough copies to exceed L2, so every
+    launch streams its weights from HBM.  Reports GB/s (algorithmic bytes) per shape."""
+    import torch
+    from wedlm_b200 import Context
+    hbm, _, peak_kind = peaks()
+    ctx = Context(None, device=local)
+    M = 96
+    X = torch.randn(M, 12288, device="cuda").to(torch.bfloat16)
+    res = {}
+    total_bytes, total_ms = 0.0, 0.0
+    only = set(args.gemm_only.split(",")) if args.gemm_only else None
+    for name, N, K, epi in GEMM_SHAPES_8B:
+        if only and name not in only:
+            continue
+        nW = 2 if epi == 3 else 1
+        wbytes = nW * N * K * 2
+        R = max(1, -(-300_000_000 // wbytes)) if not args.profile else 1
+        Ws = [[ctx.pack_weight(torch.randn(N, K, device="cuda").mul_(K ** -0.5).to(torch.bfloat16))
+               for _ in range(nW)] for _ in range(R)]
+        out = torch.zeros(M, N, device="cuda", dtype=torch.bfloat16)
+        Xs = X[:, :K]
+        def f(i):
+            W = Ws[i % R]
+            ctx.gemm(Xs, W[0], out, epi, W2=W[1] if nW == 2 else None, N=N,
+                     resid=out if epi == 2 else None)
+        for i in range(max(args.warmup, R)):
+            f(i)
+        torch.cuda.synchronize()
+        n = args.steps if args.profile else max(args.steps, 2 * R)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if args.profile:
+            e0.record()
+            for i in range(n):
+                f(i)
+            e1.record()
+        else:
+            # replay the launches from a CUDA graph so host overhead does not gap them
+            side = torch.cuda.Stream()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(side):
+                with torch.cuda.graph(g, stream=side):
+                    for i in range(n):
+                        f(i)
+            g.replay()
+            torch.cuda.synchronize()
+            e0.record()
+            g.replay()
+            e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / n
+        byt = wbytes + M * K * 2 + M * N * 2 * (2 if epi == 2 else 1)
+        res[name] = {"N": N, "K": K, "us": round(ms * 1e3, 2), "GBps": round(byt / ms / 1e6, 1),
+                     "frac": round(byt / ms / 1e6 / hbm, 4)}
+        total_bytes += byt
+        total_ms += ms
+        del Ws
+        torch.cuda.empty_cache()
+    ctx.check_device_error()
+    ctx.close()
+    achieved = total_bytes / total_ms / 1e6
+    return {"metric": METRIC, "value": round(achieved, 1), "unit": "GB/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "config": {"workload": "gemm_shapes: the five projection GEMMs "
+                                                        "of one 8B decode step at M = 96", "shapes": res,
+                                            "l2": "weights rotated over > 300 MB of copies"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / hbm, 4)}}
+
+
+# ----------------------------------------------------------------------------------
 PROMPT_8B, NEW_8B, WINDOW_8B = 512, 512, 96
 
 
@@ -352,9 +430,10 @@ def bench_decode_8b(args, rank, ws, local):
     prompt = make_prompt(PROMPT_8B, seed=rank)
     params = balanced_params()
     stream = torch.cuda.current_stream()
-    # warm the kernels, tensor maps and scratch on a short run
-    ctx.generate_streaming(prompt[:64], 8, WINDOW_8B, params)
-    torch.cuda.synchronize()
+    if not args.profile:
+        # warm the kernels, tensor maps and scratch on a short run
+        ctx.generate_streaming(prompt[:64], 8, WINDOW_8B, params)
+        torch.cuda.synchronize()
 
     need = args.warmup + args.steps + args.profile_steps
     assert need < NEW_8B, "steps exceed one 512-token generation"
@@ -399,6 +478,11 @@ def bench_decode_8b(args, rank, ws, local):
     ctx.profile_enable(False)
     ctx.decode_end()
 
+    if args.profile:
+        ctx.close()
+        return {"metric": METRIC, "value": round(value, 2), "unit": "committed tok/s",
+                "ms_per_step": round(ms_max, 3), "kernel_classes": prof,
+                "note": "profiling run (no e2e)"}
     # end to end through the public generate call: prompt from host, ids back to host
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(ws)
@@ -568,7 +652,9 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="decode_8b", choices=["decode_8b", "entropy_select"])
+    ap.add_argument("--workload", default="decode_8b",
+                    choices=["decode_8b", "entropy_select", "gemm_shapes"])
+    ap.add_argument("--gemm-only", default="", help="comma list of gemm_shapes names")
     ap.add_argument("--profile-steps", type=int, default=10,
                     help="decode steps timed per kernel class after the headline region")
     ap.add_argument("--no-entropy", action="store_true",
@@ -596,6 +682,8 @@ def main():
     rank, ws, local = dist_setup(args.gpus)
     if args.workload == "decode_8b":
         line = bench_decode_8b(args, rank, ws, local)
+    elif args.workload == "gemm_shapes":
+        line = bench_gemm_shapes(args, rank, ws, local)
     else:
         line = bench_entropy_select(args, rank, ws, local)
     if rank == 0:

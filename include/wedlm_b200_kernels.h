@@ -25,11 +25,20 @@ enum wedlm_gemm_epilogue {
 /* Y[m, n] = sum_k X[m, k] * W[n, k] (Linear::forward without bias) plus epilogue.
  * All pointers are device pointers of `dtype` (WEDLM_BF16: tcgen05 tensor cores,
  * K % 64 == 0, 16-byte aligned rows; WEDLM_F32: CUDA cores).  Row strides are in
- * elements.  `resid` may alias `out`. */
+ * elements.  `resid` may alias `out`.  w_layout 0: W (and W2) row-major with stride ldw;
+ * w_layout 1 (bf16 only): W and W2 packed by wedlm_kernel_pack_weight. */
 WEDLM_API int wedlm_kernel_gemm(wedlm_ctx* ctx, const void* X, int64_t ldx, const void* W,
-                                const void* W2, int64_t ldw, int M, int N, int K, int dtype,
-                                int epilogue, void* out, int64_t ldo, const void* resid,
-                                int64_t ldr, void* stream);
+                                const void* W2, int64_t ldw, int w_layout, int M, int N, int K,
+                                int dtype, int epilogue, void* out, int64_t ldo,
+                                const void* resid, int64_t ldr, void* stream);
+
+/* Pack a row-major bf16 weight [N, K] (row stride ld, K % 64 == 0) into GEMM tiles:
+ * `packed` (device, 16-byte aligned) must hold ceil(N / 128) * 128 * K elements; rows
+ * past N are left as they are (zero them first).  Tile (n_tile, k-block) of 128 rows x
+ * 64 columns is one contiguous 16 KB block holding the 128-byte-swizzled image the tensor
+ * cores read, so the GEMM streams each pipeline stage with one sequential bulk copy. */
+WEDLM_API int wedlm_kernel_pack_weight(wedlm_ctx* ctx, const void* W, int64_t ld, int N, int K,
+                                       void* packed, void* stream);
 
 /* Synchronises `stream`, then reports (and clears) a device-side wait that gave up
  * inside a kernel since the last check: WEDLM_ERR_TIMEOUT, else WEDLM_OK. */

@@ -47,6 +47,11 @@ def test_store_bf16(ctx, M, N, K):
     ctx.gemm(X, W, out, ctx.EPI_STORE)
     ctx.check_device_error()
     check_close(out, X.float() @ W.float().T)
+    # packed weight tiles (1-D bulk-copy path) give the same result bit for bit
+    outp = torch.empty_like(out)
+    ctx.gemm(X, ctx.pack_weight(W), outp, ctx.EPI_STORE, N=N)
+    ctx.check_device_error()
+    assert torch.equal(out, outp)
 
 
 @pytest.mark.parametrize("M,N,K", [(96, 151936, 4096), (33, 640, 256)])
@@ -80,6 +85,9 @@ def test_swiglu(ctx, M, N, K):
     out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
     ctx.gemm(X, Wg, out, ctx.EPI_SWIGLU, W2=Wu)
     ctx.check_device_error()
+    outp = torch.empty_like(out)
+    ctx.gemm(X, ctx.pack_weight(Wg), outp, ctx.EPI_SWIGLU, W2=ctx.pack_weight(Wu), N=N)
+    assert torch.equal(out, outp)
     # unrounded f32 reference: the kernel rounds gate, up, silu and the product to bf16
     # as the reference does (three roundings of 2^-9 each), hence rtol 2^-6
     g = X.float() @ Wg.float().T

@@ -293,14 +293,17 @@ int wedlm_entropy_combine(wedlm_ctx* ctx, const float* partials, int nshards, in
 }  // extern "C"
 
 extern "C" int wedlm_kernel_gemm(wedlm_ctx* ctx, const void* X, int64_t ldx, const void* W,
-                                 const void* W2, int64_t ldw, int M, int N, int K, int dtype,
-                                 int epilogue, void* out, int64_t ldo, const void* resid,
-                                 int64_t ldr, void* stream) {
+                                 const void* W2, int64_t ldw, int w_layout, int M, int N, int K,
+                                 int dtype, int epilogue, void* out, int64_t ldo,
+                                 const void* resid, int64_t ldr, void* stream) {
   if (!ctx) return WEDLM_ERR_INVALID_ARG;
   if (int rc = set_device(ctx)) return rc;
   wedlm::GemmArgs a;
   a.X = X; a.ldx = ldx; a.W = W; a.W2 = W2; a.ldw = ldw;
   a.M = M; a.N = N; a.K = K; a.epi = epilogue;
+  a.w_packed = w_layout == 1;
+  if (w_layout == 1 && dtype != WEDLM_BF16)
+    return ctx->fail(Status::err(WEDLM_ERR_INVALID_ARG, "packed weights are bf16 only"));
   a.out = out; a.ldo = ldo; a.resid = resid; a.ldr = ldr;
   if (M <= 0 || N <= 0 || K <= 0 || !X || !W || !out || epilogue < 0 || epilogue > 3)
     return ctx->fail(Status::err(WEDLM_ERR_INVALID_ARG, "bad GEMM arguments"));
@@ -359,4 +362,14 @@ extern "C" int wedlm_launch_count(const wedlm_ctx* ctx, int64_t* out) {
   if (!ctx || !out) return WEDLM_ERR_INVALID_ARG;
   *out = ctx->launches;
   return WEDLM_OK;
+}
+
+extern "C" int wedlm_kernel_pack_weight(wedlm_ctx* ctx, const void* W, int64_t ld, int N, int K,
+                                        void* packed, void* stream) {
+  if (!ctx) return WEDLM_ERR_INVALID_ARG;
+  if (int rc = set_device(ctx)) return rc;
+  if (!W || !packed || N <= 0 || K <= 0 || K % 64 != 0 || (uintptr_t)packed % 16 != 0)
+    return ctx->fail(Status::err(WEDLM_ERR_INVALID_ARG, "bad pack arguments"));
+  Status s = wedlm::pack_weight(W, ld, 0, N, K, packed, (cudaStream_t)stream);
+  return s.good() ? WEDLM_OK : ctx->fail(s);
 }

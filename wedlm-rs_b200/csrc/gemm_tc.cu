@@ -23,6 +23,7 @@
 //                 bf16 or f32 stores, or partial publication for shared tiles.
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -37,26 +38,33 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kThreadsTC = 192;
+constexpr int kThreadsTC = 192;  // 6 warps: TMA producer, MMA issuer, 4 epilogue
 constexpr int kBK = 64;              // K elements per stage (128 bytes of bf16)
 constexpr int kTileN = 128;          // weight rows per tile (MMA M)
 constexpr int kATileBytes = kTileN * kBK * 2;
 
 struct TcParams {
   int N, M, K;
-  int n_tiles, t_tiles, kb_total;
+  int n_tiles, t_tiles, kb_total;  // kb_total: k-steps per tile (each ks 64-wide k-blocks)
+  int ks, kb64;                     // k-blocks per step, 64-wide k-blocks per row
   long iters;          // tiles * kb_total
   int grid;
   int tok_tile;
   int epi, dual;
   int stages, nbuf;
-  uint32_t stage_bytes, tmem_cols, acc_cols;
+  uint32_t stage_bytes, tmem_cols, acc_cols;  // stage: ks k-blocks of weights + activations
   void* out;
   int ldo;
   const __nv_bfloat16* resid;
   int ldr;
   float* ws;           // [grid][2 slots][na][tok_tile][128 weight rows]
   int* err;
+  const uint8_t* wp;   // packed weight tiles (when packed)
+  const uint8_t* wp2;
+  int packed;
+  float* slots;        // slot mode: [tiles][maxc][na][tok_tile][128]
+  int slot_mode, maxc;
+  int poll, nohint;   // tuning: spin on test_wait; plain bulk copies without L2 hint
   int vec_ok;          // out / resid rows 16-byte aligned
 };
 
@@ -171,13 +179,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.stages * p.stage_bytes);
+  // layout: stage ring | barriers (<= 1 KB) | epilogue transpose buffers
+  uint8_t* tail = smem + p.stages * p.stage_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(tail);
   uint64_t* empty = full + p.stages;
   uint64_t* acc_full = empty + p.stages;   // [2]
   uint64_t* acc_empty = acc_full + 2;      // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   // per-epilogue-warp transpose buffers: [2 accumulators][16 tokens][33]
-  float* tbuf = reinterpret_cast<float*>(smem + p.stages * p.stage_bytes + 1024);
+  float* tbuf = reinterpret_cast<float*>(tail + 1024);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cta = blockIdx.x;
@@ -203,26 +213,42 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---------------- TMA producer ----------------
-      tma_prefetch_desc(&tmW);
+      // ---------------- TMA producer: weights (bulk) and activations ----------------
       tma_prefetch_desc(&tmX);
-      if (p.dual) tma_prefetch_desc(&tmW2);
-      const uint64_t pol_w = policy_evict_first();
-      const uint32_t a_bytes = kATileBytes * (p.dual ? 2 : 1);
+      if (!p.packed) {
+        tma_prefetch_desc(&tmW);
+        if (p.dual) tma_prefetch_desc(&tmW2);
+      }
+      const uint64_t pol_w = p.nohint ? policy_evict_last() : policy_evict_first();
+      const uint32_t wbytes = (uint32_t)(p.ks * kATileBytes);
+      const uint32_t a_bytes = wbytes * (p.dual ? 2 : 1);
       long issued = 0;
       for (long it = beg; it < end; ++it) {
         const long i = it - beg;
         const int s = (int)(i % p.stages);
         const uint32_t ph = (uint32_t)(i / p.stages) & 1u;
-        if (!mbar_wait(empty + s, ph ^ 1u, p.err, kErrWaitEmpty)) break;
+        if (!(p.poll ? mbar_spin(empty + s, ph ^ 1u, p.err, kErrWaitEmpty)
+                     : mbar_wait(empty + s, ph ^ 1u, p.err, kErrWaitEmpty)))
+          break;
         issued = i + 1;
-        const int tile = (int)(it / p.kb_total), kb = (int)(it % p.kb_total);
+        const int tile = (int)(it / p.kb_total), kb = (int)(it % p.kb_total) * p.ks;
         const int n0 = (tile / p.t_tiles) * kTileN, t0 = (tile % p.t_tiles) * p.tok_tile;
         uint8_t* st = smem + s * p.stage_bytes;
         mbar_arrive_expect_tx(full + s, p.stage_bytes);
-        tma_load_2d_hint(st, &tmW, full + s, kb * kBK, n0, pol_w);
-        if (p.dual) tma_load_2d_hint(st + kATileBytes, &tmW2, full + s, kb * kBK, n0, pol_w);
-        tma_load_2d(st + a_bytes, &tmX, full + s, kb * kBK, t0);
+        if (p.packed) {
+          // the ks k-blocks of this step are contiguous in the packed layout
+          const long blk = ((long)(tile / p.t_tiles) * p.kb64 + kb) * kATileBytes;
+          bulk_load_hint(st, p.wp + blk, wbytes, full + s, pol_w);
+          if (p.dual) bulk_load_hint(st + wbytes, p.wp2 + blk, wbytes, full + s, pol_w);
+        } else {
+          for (int j = 0; j < p.ks; ++j) {
+            tma_load_2d_hint(st + j * kATileBytes, &tmW, full + s, (kb + j) * kBK, n0, pol_w);
+            if (p.dual)
+              tma_load_2d_hint(st + wbytes + j * kATileBytes, &tmW2, full + s, (kb + j) * kBK, n0, pol_w);
+          }
+        }
+        for (int j = 0; j < p.ks; ++j)
+          tma_load_2d(st + a_bytes + j * p.tok_tile * kBK * 2, &tmX, full + s, (kb + j) * kBK, t0);
       }
       // drain: wait for the last load issued to every stage before the CTA may exit
       for (long s = 0; s < p.stages && s < issued; ++s) {
@@ -234,7 +260,6 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
       const uint32_t idesc = idesc_bf16_f32(kTileN, p.tok_tile);
-      const uint32_t a_bytes = kATileBytes * (p.dual ? 2 : 1);
       bool ok = true;
       int nseg = 0;
       for (long it = beg; it < end && ok;) {
@@ -248,23 +273,29 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
         for (long j = sg.it0; j < sg.it1; ++j) {
           const long i = j - beg;
           const int s = (int)(i % p.stages);
-          if (!mbar_wait(full + s, (uint32_t)(i / p.stages) & 1u, p.err, kErrWaitFull)) {
+          if (!(p.poll ? mbar_spin(full + s, (uint32_t)(i / p.stages) & 1u, p.err, kErrWaitFull)
+                       : mbar_wait(full + s, (uint32_t)(i / p.stages) & 1u, p.err, kErrWaitFull))) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + s * p.stage_bytes);
-          const uint32_t sb = sa + a_bytes;
+          const uint32_t wbytes = (uint32_t)(p.ks * kATileBytes);
+          const uint32_t sb = sa + wbytes * (p.dual ? 2 : 1);
+          for (int jb = 0; jb < p.ks; ++jb) {
+            const uint32_t ja = sa + jb * kATileBytes, jx = sb + jb * p.tok_tile * kBK * 2;
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
-            const bool accum = (j != sg.it0) || (kk != 0);
-            const uint64_t bd = smem_desc_sw128(sb + kk * 32);
-            tc_mma_f16(acc, smem_desc_sw128(sa + kk * 32), bd, idesc, accum);
-            if (p.dual)
-              tc_mma_f16(acc + (uint32_t)p.tok_tile, smem_desc_sw128(sa + kATileBytes + kk * 32),
-                         bd, idesc, accum);
+            for (int kk = 0; kk < kBK / 16; ++kk) {
+              const bool accum = (j != sg.it0) || (jb != 0) || (kk != 0);
+              const uint64_t bd = smem_desc_sw128(jx + kk * 32);
+              tc_mma_f16(acc, smem_desc_sw128(ja + kk * 32), bd, idesc, accum);
+              if (p.dual)
+                tc_mma_f16(acc + (uint32_t)p.tok_tile, smem_desc_sw128(ja + wbytes + kk * 32), bd,
+                           idesc, accum);
+            }
           }
           tc_commit(empty + s);
+          if (!ok) break;
         }
         tc_commit(acc_full + buf);
         it = sg.it1;
@@ -289,8 +320,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
       // shared tile: publish this CTA's partial in slot 0 (its first segment) or slot 1
       // (its last), layout [na][tok_tile][128 weight rows] f32; the reduce kernel sums
       // the contributors of every shared tile.
-      const int slot = (sg.it0 == beg) ? 0 : 1;
-      float* part = p.ws + ((long)cta * 2 + slot) * slot_floats;
+      float* part;
+      if (p.slot_mode) {
+        const int rank = cta - owner_cta((long)sg.tile * p.kb_total, p.iters, p.grid);
+        part = p.slots + ((long)sg.tile * p.maxc + rank) * slot_floats;
+      } else {
+        part = p.ws + ((long)cta * 2 + ((sg.it0 == beg) ? 0 : 1)) * slot_floats;
+      }
       float* tb = tbuf + (warp - 2) * (2 * 16 * 33);
       const int jt = lane >> 1, hh = (lane & 1) * 16;   // transposed view: token, row half
       for (int c = 0; c < p.tok_tile; c += 16) {
@@ -311,7 +347,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
         }
         __syncwarp();
         const int rr = q * 32 + hh;  // first of this lane's 16 weight rows in the tile
-        if (sg.full) {
+        if (sg.full && !p.slot_mode) {
           if (ok && c + jt < tok_end) epilogue_store_vec<16>(p, t0 + c + jt, n0 + rr, o, o2);
         } else {
           float* dst = part + (long)(c + jt) * kTileN + rr;
@@ -446,6 +482,94 @@ void forget_tensor_maps() {
   c.maps.clear();
 }
 
+// ---- packed weights ---------------------------------------------------------------------
+namespace {
+
+__device__ __forceinline__ long packed_index(long gr, long c, long kb_total) {
+  const long tile = gr >> 7, r = gr & 127, kb = c >> 6, cc = c & 63;
+  return ((tile * kb_total + kb) * 128 + r) * 64 + (((cc >> 3) ^ (r & 7)) << 3) + (cc & 7);
+}
+
+// one thread per 8 consecutive columns (16 bytes)
+__global__ void pack_kernel(const __nv_bfloat16* src, long ld, long row_off, long rows, long K,
+                            __nv_bfloat16* P, int unpack) {
+  const long chunks = rows * (K / 8);
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < chunks; i += (long)gridDim.x * blockDim.x) {
+    const long r = i / (K / 8), c = (i % (K / 8)) * 8;
+    const long pi = packed_index(row_off + r, c, K / 64);
+    if (unpack)
+      *reinterpret_cast<uint4*>(const_cast<__nv_bfloat16*>(src) + r * ld + c) =
+          *reinterpret_cast<const uint4*>(P + pi);
+    else
+      *reinterpret_cast<uint4*>(P + pi) = *reinterpret_cast<const uint4*>(src + r * ld + c);
+  }
+}
+
+__device__ __forceinline__ uint64_t mix64d(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+__global__ void init_packed_kernel(__nv_bfloat16* P, long row_off, long rows, long K, uint64_t seed,
+                                   uint64_t tensor_id, long hash_off, float stdv) {
+  const long n = rows * K;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const long r = i / K, c = i % K;
+    const uint64_t h = mix64d(seed ^ mix64d((tensor_id << 44) + (uint64_t)(i + hash_off) + 1));
+    const float u1 = ((float)(uint32_t)(h >> 40) + 1.f) * (1.f / 16777216.f);
+    const float u2 = (float)(uint32_t)(h & 0xFFFFFF) * (1.f / 16777216.f);
+    const float z = sqrtf(-2.f * logf(u1)) * cospif(2.f * u2);
+    P[packed_index(row_off + r, c, K / 64)] = __float2bfloat16_rn(z * stdv);
+  }
+}
+
+}  // namespace
+
+long packed_weight_elems(long N, long K) { return ((N + 127) / 128) * 128 * K; }
+
+Status pack_weight(const void* src, long ld, long row_off, long rows, long K, void* packed,
+                   cudaStream_t st) {
+  WEDLM_CHECK_ARG(K % 64 == 0 && ld % 8 == 0 && ((uintptr_t)src % 16) == 0, "bad pack layout");
+  if (rows <= 0) return Status::ok();
+  pack_kernel<<<1184, 256, 0, st>>>((const __nv_bfloat16*)src, ld, row_off, rows, K,
+                                    (__nv_bfloat16*)packed, 0);
+  WEDLM_CUDA_TRY(cudaGetLastError());
+  return Status::ok();
+}
+
+Status unpack_weight(const void* packed, long row_off, long rows, long K, void* dst,
+                     cudaStream_t st) {
+  WEDLM_CHECK_ARG(K % 64 == 0 && ((uintptr_t)dst % 16) == 0, "bad unpack layout");
+  if (rows <= 0) return Status::ok();
+  pack_kernel<<<1184, 256, 0, st>>>((const __nv_bfloat16*)dst, K, row_off, rows, K,
+                                    (__nv_bfloat16*)packed, 1);
+  WEDLM_CUDA_TRY(cudaGetLastError());
+  return Status::ok();
+}
+
+Status init_normal_packed(void* packed, long row_off, long rows, long K, uint64_t seed,
+                          uint64_t tensor_id, long hash_off, float stdv, cudaStream_t st) {
+  WEDLM_CHECK_ARG(K % 64 == 0, "bad packed layout");
+  init_packed_kernel<<<1184, 256, 0, st>>>((__nv_bfloat16*)packed, row_off, rows, K, seed,
+                                           tensor_id, hash_off, stdv);
+  WEDLM_CUDA_TRY(cudaGetLastError());
+  return Status::ok();
+}
+
+PartialSet partial_set(const GemmPlan& g, const float* slots, bool dual) {
+  PartialSet ps;
+  ps.slots = slots;
+  ps.iters = (long)g.n_tiles * g.t_tiles * g.kb_total;
+  ps.grid = g.grid;
+  ps.kb_total = g.kb_total;
+  ps.t_tiles = g.t_tiles;
+  ps.tok_tile = g.tok_tile;
+  ps.maxc = g.maxc;
+  ps.na = dual ? 2 : 1;
+  return ps;
+}
+
 GemmPlan plan_gemm_tc(int M, int N, int K, bool dual, int num_sms) {
   GemmPlan g;
   int tt = ((M + 15) / 16) * 16;
@@ -457,14 +581,27 @@ GemmPlan plan_gemm_tc(int M, int N, int K, bool dual, int num_sms) {
   g.tok_tile = tt < 16 ? 16 : tt;
   g.t_tiles = (M + g.tok_tile - 1) / g.tok_tile;
   g.n_tiles = (N + kTileN - 1) / kTileN;
-  g.kb_total = K / kBK;
+  // k-blocks per pipeline stage: larger bulk copies per stage stream faster; keep >= 2
+  // stages and enough k-steps per tile for the stream-K split
+  const int kb64 = K / kBK;
+  int ks = 1;
+  if (const char* e = getenv("WEDLM_GEMM_KS")) ks = atoi(e);
+  else ks = 4;  // largest stage that still leaves two stages in the budget (see below)
+  while (ks > 1 && (kb64 % ks != 0)) ks >>= 1;
+  if (ks < 1) ks = 1;
+  while (ks > 1 && 2u * ks * (kATileBytes * (dual ? 2 : 1) +
+                              (M > 256 ? 256 : ((M + 15) / 16) * 16) * kBK * 2) > 192u * 1024u)
+    ks >>= 1;
+  g.ks = ks;
+  g.kb64 = kb64;
+  g.kb_total = kb64 / ks;
   const long iters = (long)g.n_tiles * g.t_tiles * g.kb_total;
   g.grid = (int)(iters < num_sms ? iters : num_sms);
   g.splits = 1;
-  g.stage_bytes = (uint32_t)(kATileBytes * (dual ? 2 : 1) + g.tok_tile * kBK * 2);
+  g.stage_bytes = (uint32_t)(ks * (kATileBytes * (dual ? 2 : 1) + g.tok_tile * kBK * 2));
   const uint32_t budget = 192 * 1024;
   int st = (int)(budget / g.stage_bytes);
-  g.stages = st > 8 ? 8 : (st < 2 ? 2 : st);
+  g.stages = st > 16 ? 16 : (st < 2 ? 2 : st);
   g.acc_cols = (uint32_t)(g.tok_tile * (dual ? 2 : 1));
   g.nbuf = g.acc_cols * 2 <= 512 ? 2 : 1;
   uint32_t tc = 32;
@@ -473,6 +610,11 @@ GemmPlan plan_gemm_tc(int M, int N, int K, bool dual, int num_sms) {
   // stages | barriers (<= 1 KB) | epilogue transpose buffers (4 warps x 2 x 16 x 33 f32)
   g.smem_bytes = 1024 + g.stages * g.stage_bytes + 1024 + 4 * 2 * 16 * 33 * 4;
   g.ws_floats = (long)g.grid * 2 * (dual ? 2 : 1) * g.tok_tile * kTileN;
+  // most CTAs a tile can be shared by: ceil(kb_total / (iters / grid)) + 1
+  const long per = iters / g.grid;
+  g.maxc = (int)((g.kb_total + per - 1) / (per > 0 ? per : 1)) + 1;
+  if (g.maxc > g.grid) g.maxc = g.grid;
+  g.slot_floats = (long)g.n_tiles * g.t_tiles * g.maxc * (dual ? 2 : 1) * g.tok_tile * kTileN;
   g.counters = 0;
   return g;
 }
@@ -481,14 +623,21 @@ Status run_gemm_tc(const GemmArgs& a, const GemmPlan& g, float* ws, unsigned* co
                    cudaStream_t st) {
   WEDLM_CHECK_ARG(a.K % kBK == 0, "tcgen05 GEMM needs K % 64 == 0");
   WEDLM_CHECK_ARG(a.M > 0 && a.N > 0, "empty GEMM");
-  WEDLM_CHECK_ARG(ws != nullptr, "the GEMM needs its workspace");
+  WEDLM_CHECK_ARG(ws != nullptr || a.slots != nullptr, "the GEMM needs its workspace");
   (void)counters;
   const bool dual = a.epi == EPI_SWIGLU_BF16;
   WEDLM_CHECK_ARG(!dual || a.W2, "SwiGLU GEMM needs the second weight matrix");
   CUtensorMap mW, mW2, mX;
-  WEDLM_TRY(cached_tmap(&mW, a.W, a.N, a.K, a.ldw, kTileN));
-  WEDLM_TRY(cached_tmap(&mW2, dual ? a.W2 : a.W, a.N, a.K, a.ldw, kTileN));
   WEDLM_TRY(cached_tmap(&mX, a.X, a.M, a.K, a.ldx, g.tok_tile));
+  if (a.w_packed) {
+    WEDLM_CHECK_ARG(((uintptr_t)a.W % 16 == 0) && (!dual || (uintptr_t)a.W2 % 16 == 0),
+                    "packed weights must be 16-byte aligned");
+    mW = mX;
+    mW2 = mX;
+  } else {
+    WEDLM_TRY(cached_tmap(&mW, a.W, a.N, a.K, a.ldw, kTileN));
+    WEDLM_TRY(cached_tmap(&mW2, dual ? a.W2 : a.W, a.N, a.K, a.ldw, kTileN));
+  }
   TcParams p;
   p.N = a.N;
   p.M = a.M;
@@ -496,6 +645,8 @@ Status run_gemm_tc(const GemmArgs& a, const GemmPlan& g, float* ws, unsigned* co
   p.n_tiles = g.n_tiles;
   p.t_tiles = g.t_tiles;
   p.kb_total = g.kb_total;
+  p.ks = g.ks;
+  p.kb64 = g.kb64;
   p.iters = (long)g.n_tiles * g.t_tiles * g.kb_total;
   p.grid = g.grid;
   p.tok_tile = g.tok_tile;
@@ -512,6 +663,14 @@ Status run_gemm_tc(const GemmArgs& a, const GemmPlan& g, float* ws, unsigned* co
   p.ldr = (int)a.ldr;
   p.ws = ws;
   p.err = err;
+  p.wp = reinterpret_cast<const uint8_t*>(a.W);
+  p.wp2 = reinterpret_cast<const uint8_t*>(dual ? a.W2 : a.W);
+  p.packed = a.w_packed ? 1 : 0;
+  p.slots = a.slots;
+  p.slot_mode = a.slots ? 1 : 0;
+  p.maxc = g.maxc;
+  p.poll = getenv("WEDLM_GEMM_POLL") ? atoi(getenv("WEDLM_GEMM_POLL")) : 0;
+  p.nohint = getenv("WEDLM_GEMM_NOHINT") ? atoi(getenv("WEDLM_GEMM_NOHINT")) : 0;
   const int osz = a.epi == EPI_STORE_F32 ? 4 : 2;
   p.vec_ok = ((uintptr_t)a.out % 16 == 0) && ((a.ldo * osz) % 16 == 0) &&
              (a.epi != EPI_RESID_BF16 || (((uintptr_t)a.resid % 16 == 0) && (a.ldr * 2) % 16 == 0));
@@ -525,7 +684,7 @@ Status run_gemm_tc(const GemmArgs& a, const GemmPlan& g, float* ws, unsigned* co
   }
   gemm_tc_kernel<<<(unsigned)g.grid, kThreadsTC, g.smem_bytes, st>>>(mW, mW2, mX, p);
   WEDLM_CUDA_TRY(cudaGetLastError());
-  if (g.grid > 1) {
+  if (g.grid > 1 && !p.slot_mode) {
     gemm_reduce_kernel<<<(unsigned)(g.grid - 1), 256, 0, st>>>(p);
     WEDLM_CUDA_TRY(cudaGetLastError());
   }

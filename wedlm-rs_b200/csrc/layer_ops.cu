@@ -8,6 +8,8 @@
 // its output.
 #include "layer_ops.h"
 
+#include <algorithm>
+
 namespace wedlm {
 
 namespace {
@@ -70,7 +72,8 @@ __global__ void rmsnorm_kernel(const T* __restrict__ x, long ldx, const float* _
 // dim d = 32 * E; lane holds elements lane*E .. lane*E+E-1; the rotate-half partner of
 // element i (i +/- d/2) sits in lane ^ 16 at the same slot.
 template <typename T, int E>
-__global__ void rope_kv_kernel(RopeKvArgs a) {
+__global__ void rope_kv_kernel(RopeKvArgs a, PartialSet ps_val) {
+  if (a.qkv_partials != nullptr) a.qkv_partials = &ps_val;
   const int warps = blockDim.x >> 5;
   const int gw = blockIdx.x * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -78,10 +81,29 @@ __global__ void rope_kv_kernel(RopeKvArgs a) {
   if (gw >= a.rows * heads) return;
   const int r = gw / heads, hh = gw % heads;
   const int d = 32 * E;
-  const T* src = reinterpret_cast<const T*>(a.qkv) + (long)r * a.ld_qkv + (long)hh * d;
   float x[E];
+  if (a.qkv_partials != nullptr) {
+    // projection output rounded to the model dtype, as the reference's Linear returns it
+    if (E % 4 == 0) {
 #pragma unroll
-  for (int e = 0; e < E; ++e) x[e] = to_f32(src[lane * E + e]);
+      for (int e = 0; e < E; e += 4) {
+        const PsTile t = ps_tile(*a.qkv_partials, r, hh * d + lane * E + e, 0);
+        const float4 v = ps_sum4(t);
+        x[e] = to_f32(rnd<T>(v.x));
+        x[e + 1] = to_f32(rnd<T>(v.y));
+        x[e + 2] = to_f32(rnd<T>(v.z));
+        x[e + 3] = to_f32(rnd<T>(v.w));
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < E; ++e)
+        x[e] = to_f32(rnd<T>(ps_sum(*a.qkv_partials, r, hh * d + lane * E + e, 0)));
+    }
+  } else {
+    const T* src = reinterpret_cast<const T*>(a.qkv) + (long)r * a.ld_qkv + (long)hh * d;
+#pragma unroll
+    for (int e = 0; e < E; ++e) x[e] = to_f32(src[lane * E + e]);
+  }
   const bool is_q = hh < a.nh, is_k = !is_q && hh < a.nh + a.nkv;
   if (is_q || is_k) {
     if (a.qk_norm) {
@@ -181,7 +203,104 @@ __global__ void attention_f32_kernel(AttnArgs a) {
   for (int k = 0; k * 32 + lane < d; ++k) o[k * 32 + lane] = acc[k] / l;
 }
 
+// ---- residual add (from split-K partials) fused with the next RMSNorm ----------------
+__global__ void __launch_bounds__(512)
+resid_norm_kernel(__nv_bfloat16* h, PartialSet ps, int has_ps, const float* __restrict__ w,
+                  int H, float eps, __nv_bfloat16* xn) {
+  extern __shared__ float srow[];
+  const int r = blockIdx.x;
+  __nv_bfloat16* hr = h + (long)r * H;
+  float ss = 0.f;
+  for (int i = threadIdx.x * 4; i < H; i += blockDim.x * 4) {
+    const uint2 hw = *reinterpret_cast<const uint2*>(hr + i);
+    float v[4] = {bf16_lo(hw.x), bf16_hi(hw.x), bf16_lo(hw.y), bf16_hi(hw.y)};
+    if (has_ps) {
+      const float4 y = ps_sum4(ps_tile(ps, r, i, 0));
+      const float ys[4] = {y.x, y.y, y.z, y.w};
+      uint32_t o[2];
+#pragma unroll
+      for (int k = 0; k < 4; k += 2) {
+        const float a0 = __bfloat162float(__float2bfloat16_rn(v[k] + __bfloat162float(__float2bfloat16_rn(ys[k]))));
+        const float a1 = __bfloat162float(__float2bfloat16_rn(v[k + 1] + __bfloat162float(__float2bfloat16_rn(ys[k + 1]))));
+        v[k] = a0;
+        v[k + 1] = a1;
+        const __nv_bfloat162 h2 = __floats2bfloat162_rn(a0, a1);
+        o[k / 2] = *reinterpret_cast<const uint32_t*>(&h2);
+      }
+      *reinterpret_cast<uint2*>(hr + i) = make_uint2(o[0], o[1]);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      srow[i + k] = v[k];
+      ss = fmaf(v[k], v[k], ss);
+    }
+  }
+  __shared__ float sh[32];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? sh[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) sh[0] = v;
+  }
+  __syncthreads();
+  const float denom = sqrtf(sh[0] / (float)H + eps);
+  __nv_bfloat16* xr = xn + (long)r * H;
+  for (int i = threadIdx.x * 4; i < H; i += blockDim.x * 4) {
+    const __nv_bfloat162 a = __floats2bfloat162_rn((srow[i] / denom) * w[i], (srow[i + 1] / denom) * w[i + 1]);
+    const __nv_bfloat162 b = __floats2bfloat162_rn((srow[i + 2] / denom) * w[i + 2], (srow[i + 3] / denom) * w[i + 3]);
+    *reinterpret_cast<uint2*>(xr + i) =
+        make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+  }
+}
+
+// ---- SwiGLU from the gate/up partials ---------------------------------------------------
+__global__ void swiglu_kernel(PartialSet ps, int rows, int I, __nv_bfloat16* act) {
+  const long n4 = (long)rows * I / 4;
+  for (long e4 = blockIdx.x * (long)blockDim.x + threadIdx.x; e4 < n4; e4 += (long)gridDim.x * blockDim.x) {
+    const long e = e4 * 4;
+    const int r = (int)(e / I), j = (int)(e % I);
+    const float4 g4 = ps_sum4(ps_tile(ps, r, j, 0));
+    const float4 u4 = ps_sum4(ps_tile(ps, r, j, 1));
+    const float gs[4] = {g4.x, g4.y, g4.z, g4.w}, us[4] = {u4.x, u4.y, u4.z, u4.w};
+    float y[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float g = __bfloat162float(__float2bfloat16_rn(gs[k]));
+      const float u = __bfloat162float(__float2bfloat16_rn(us[k]));
+      const float sg = __bfloat162float(__float2bfloat16_rn(g / (1.f + __expf(-g))));
+      y[k] = sg * u;
+    }
+    const __nv_bfloat162 a = __floats2bfloat162_rn(y[0], y[1]);
+    const __nv_bfloat162 b = __floats2bfloat162_rn(y[2], y[3]);
+    *reinterpret_cast<uint2*>(act + e) =
+        make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+  }
+}
+
 }  // namespace
+
+Status run_resid_norm(void* h, const PartialSet* ps, const float* w, int rows, int H, float eps,
+                      void* xn, cudaStream_t st) {
+  if (rows == 0) return Status::ok();
+  WEDLM_CHECK_ARG(H % 4 == 0, "hidden size must be a multiple of 4");
+  const PartialSet p = ps ? *ps : PartialSet();
+  resid_norm_kernel<<<rows, 512, (size_t)H * sizeof(float), st>>>(
+      (__nv_bfloat16*)h, p, ps ? 1 : 0, w, H, eps, (__nv_bfloat16*)xn);
+  WEDLM_CUDA_TRY(cudaGetLastError());
+  return Status::ok();
+}
+
+Status run_swiglu(const PartialSet& ps, int rows, int I, void* act, cudaStream_t st) {
+  if (rows == 0) return Status::ok();
+  WEDLM_CHECK_ARG(I % 4 == 0, "intermediate size must be a multiple of 4");
+  const long n4 = (long)rows * I / 4;
+  const unsigned grid = (unsigned)std::min<long>((n4 + 255) / 256, 148L * 16);
+  swiglu_kernel<<<grid, 256, 0, st>>>(ps, rows, I, (__nv_bfloat16*)act);
+  WEDLM_CUDA_TRY(cudaGetLastError());
+  return Status::ok();
+}
 
 Status run_embed(const void* table, int dtype, const int* ids, int rows, int H, int vocab,
                  void* out, int* err, cudaStream_t st) {
@@ -217,12 +336,13 @@ Status run_rope_kv(const RopeKvArgs& a, int dtype, cudaStream_t st) {
   const unsigned grid = (unsigned)((warps + per_block - 1) / per_block);
   const int E = a.head_dim / 32;
   WEDLM_CHECK_ARG(a.head_dim % 32 == 0 && E >= 1 && E <= 8, "head_dim must be 32..256, multiple of 32");
+  const PartialSet psv = a.qkv_partials ? *a.qkv_partials : PartialSet();
 #define WEDLM_ROPE_CASE(EE)                                                              \
   case EE:                                                                               \
     if (dtype == WEDLM_BF16)                                                             \
-      rope_kv_kernel<__nv_bfloat16, EE><<<grid, per_block * 32, 0, st>>>(a);            \
+      rope_kv_kernel<__nv_bfloat16, EE><<<grid, per_block * 32, 0, st>>>(a, psv);       \
     else                                                                                 \
-      rope_kv_kernel<float, EE><<<grid, per_block * 32, 0, st>>>(a);                    \
+      rope_kv_kernel<float, EE><<<grid, per_block * 32, 0, st>>>(a, psv);               \
     break;
   switch (E) {
     WEDLM_ROPE_CASE(1)

@@ -2,6 +2,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "gemm.h"
 
 namespace wedlm {
 
@@ -30,6 +31,8 @@ struct RopeKvArgs : KvGeom {
   const int* row_seq = nullptr;    // [rows] cache slot (sequence) of each row
   const int* dst_pos = nullptr;    // [rows] cache position written by each row
   void* q_out = nullptr;           // group-major [nkv][rows * group][d]
+  // bf16 models: the QKV projection as split-K partials (summed and rounded here)
+  const PartialSet* qkv_partials = nullptr;
 };
 
 struct AttnArgs : KvGeom {
@@ -51,6 +54,13 @@ Status run_embed(const void* table, int dtype, const int* ids, int rows, int H, 
 Status run_rmsnorm(const void* x, long ldx, const float* w, int rows, int H, float eps, int dtype,
                    void* out, long ldo, cudaStream_t st);
 Status run_rope_kv(const RopeKvArgs& a, int dtype, cudaStream_t st);
+// bf16: h = bf16(h + bf16(sum of partials)) (skipped when ps is NULL), then
+// xn = RMSNorm(h) * w (rounded to bf16): the residual add of layer.rs:72,78 fused with
+// the next RMSNorm (attention.rs:35-50).
+Status run_resid_norm(void* h, const PartialSet* ps, const float* w, int rows, int H, float eps,
+                      void* xn, cudaStream_t st);
+// bf16: act = bf16(silu(bf16(gate)) * bf16(up)) from the gate/up partials (mlp.rs:40-43).
+Status run_swiglu(const PartialSet& ps, int rows, int I, void* act, cudaStream_t st);
 Status run_attention_f32(const AttnArgs& a, cudaStream_t st);
 
 // bf16 block attention on the tensor cores.  The plan (work items, split-KV layout) is

@@ -109,12 +109,15 @@ float f16_bits_to_f32(uint16_t h) {
 
 // Where a named tensor lives on the device.
 struct WeightRef {
-  void* base = nullptr;  // device address of the first stored row
+  void* base = nullptr;  // device address of the first stored row (row-major), or of
+                         // the packed matrix holding the tensor (packed)
   long rows = 0;         // rows in the checkpoint tensor
   long cols = 0;
   long store_row0 = 0;   // first checkpoint row that is stored (vocab shard)
   long store_rows = 0;   // rows stored on this device
   bool is_norm = false;  // stored as f32
+  bool packed = false;   // stored as packed bf16 GEMM tiles
+  long pack_row0 = 0;    // row of the packed matrix that holds the first stored row
   int tensor_id = 0;
 };
 
@@ -142,7 +145,19 @@ Status resolve(ModelState* m, const std::string& name, WeightRef* w) {
     w->store_row0 = 0;
     w->store_rows = rows;
     w->is_norm = false;
+    w->packed = false;
+    w->pack_row0 = 0;
     w->tensor_id = id;
+  };
+  // GEMM weights of bf16 models are stored packed; `row0` = row inside the packed matrix
+  auto pmat = [&](void* pbase, long row0, long rows, long cols, int id) {
+    if (m->dt != WEDLM_BF16) {
+      mat(reinterpret_cast<uint8_t*>(pbase) + (size_t)row0 * cols * es, rows, cols, id);
+      return;
+    }
+    mat(pbase, rows, cols, id);
+    w->packed = true;
+    w->pack_row0 = row0;
   };
   auto norm = [&](float* base, long n, int id) {
     w->base = base;
@@ -158,7 +173,7 @@ Status resolve(ModelState* m, const std::string& name, WeightRef* w) {
     return Status::ok();
   }
   if (name == "lm_head.weight") {
-    mat(m->lm_head, m->V, H, 2);
+    pmat(m->lm_head, 0, m->V, H, 2);
     w->store_row0 = m->vlo;
     w->store_rows = m->vshard;
     return Status::ok();
@@ -173,15 +188,13 @@ Status resolve(ModelState* m, const std::string& name, WeightRef* w) {
     return Status::err(WEDLM_ERR_NOT_FOUND, "unknown tensor " + name);
   LayerWeights& L = m->layers[l];
   const int id0 = 16 + l * 16;
-  uint8_t* qkv = reinterpret_cast<uint8_t*>(L.wqkv);
-  if (rest == "self_attn.q_proj.weight") mat(qkv, m->qdim, H, id0 + 0);
-  else if (rest == "self_attn.k_proj.weight") mat(qkv + (size_t)m->qdim * H * es, m->kvdim, H, id0 + 1);
-  else if (rest == "self_attn.v_proj.weight")
-    mat(qkv + (size_t)(m->qdim + m->kvdim) * H * es, m->kvdim, H, id0 + 2);
-  else if (rest == "self_attn.o_proj.weight") mat(L.wo, H, m->qdim, id0 + 3);
-  else if (rest == "mlp.gate_proj.weight") mat(L.wgate, I, H, id0 + 4);
-  else if (rest == "mlp.up_proj.weight") mat(L.wup, I, H, id0 + 5);
-  else if (rest == "mlp.down_proj.weight") mat(L.wdown, H, I, id0 + 6);
+  if (rest == "self_attn.q_proj.weight") pmat(L.wqkv, 0, m->qdim, H, id0 + 0);
+  else if (rest == "self_attn.k_proj.weight") pmat(L.wqkv, m->qdim, m->kvdim, H, id0 + 1);
+  else if (rest == "self_attn.v_proj.weight") pmat(L.wqkv, m->qdim + m->kvdim, m->kvdim, H, id0 + 2);
+  else if (rest == "self_attn.o_proj.weight") pmat(L.wo, 0, H, m->qdim, id0 + 3);
+  else if (rest == "mlp.gate_proj.weight") pmat(L.wgate, 0, I, H, id0 + 4);
+  else if (rest == "mlp.up_proj.weight") pmat(L.wup, 0, I, H, id0 + 5);
+  else if (rest == "mlp.down_proj.weight") pmat(L.wdown, 0, H, I, id0 + 6);
   else if (rest == "input_layernorm.weight") norm(L.ln1, H, id0 + 7);
   else if (rest == "post_attention_layernorm.weight") norm(L.ln2, H, id0 + 8);
   else if (rest == "self_attn.q_norm.weight" && m->cfg.qk_norm) norm(L.qn, d, id0 + 9);
@@ -259,19 +272,23 @@ Status model_create(wedlm_ctx* ctx, const wedlm_config& c, int max_seqs, int max
     off = align_up(off + bytes, 256);
     return o;
   };
+  // GEMM weights of bf16 models are packed (rows padded to whole 128-row tiles)
+  auto wsize = [&](long N, long K) -> size_t {
+    return (size_t)(m->dt == WEDLM_BF16 ? packed_weight_elems(N, K) : N * K) * es;
+  };
   const size_t o_embed = take((size_t)m->V * H * es);
-  const size_t o_lm = take((size_t)m->vshard * H * es);
+  const size_t o_lm = take(wsize(m->vshard, H));
   const size_t o_fn = take((size_t)H * 4);
   struct LO {
     size_t qkv, o, g, u, dn, l1, l2, qn, kn;
   };
   std::vector<LO> lo(m->nlayers);
   for (int l = 0; l < m->nlayers; ++l) {
-    lo[l].qkv = take((size_t)m->qkvdim * H * es);
-    lo[l].o = take((size_t)H * m->qdim * es);
-    lo[l].g = take((size_t)I * H * es);
-    lo[l].u = take((size_t)I * H * es);
-    lo[l].dn = take((size_t)H * I * es);
+    lo[l].qkv = take(wsize(m->qkvdim, H));
+    lo[l].o = take(wsize(H, m->qdim));
+    lo[l].g = take(wsize(I, H));
+    lo[l].u = take(wsize(I, H));
+    lo[l].dn = take(wsize(H, I));
     lo[l].l1 = take((size_t)H * 4);
     lo[l].l2 = take((size_t)H * 4);
     lo[l].qn = take((size_t)m->d * 4);
@@ -399,6 +416,7 @@ void model_destroy(wedlm_ctx* ctx) {
   cudaFree(m->q);
   cudaFree(m->attn);
   cudaFree(m->act);
+  cudaFree(m->slots);
   cudaFree(m->d_meta);
   if (m->h_meta) cudaFreeHost(m->h_meta);
   cudaFree(m->attn_ws);
@@ -540,8 +558,11 @@ Status model_forward(wedlm_ctx* ctx, const std::vector<SeqSlice>& seqs, const in
   rk.dst_pos = d + o_dst;
   rk.q_out = m->q;
 
+  // One projection.  f32 models: CUDA-core GEMM with its epilogue.  bf16 models:
+  // tcgen05 GEMM on the packed weights; `ps` != NULL selects slot mode (split-K partials
+  // for the consumer kernel), otherwise the direct epilogue `epi` writes `out`.
   auto gemm = [&](const void* X, long ldx, const void* W, const void* W2, int N, int K, int epi,
-                  void* out, long ldo, const void* resid, long ldr, int M) -> Status {
+                  void* out, long ldo, const void* resid, long ldr, int M, PartialSet* ps) -> Status {
     GemmArgs g;
     g.X = X;
     g.ldx = ldx;
@@ -566,11 +587,27 @@ Status model_forward(wedlm_ctx* ctx, const std::vector<SeqSlice>& seqs, const in
       prof_end(ctx, st, ph, WedlmProfiler::kGemm, bytes, flops, 1);
       return s;
     }
-    GemmPlan gp = plan_gemm_tc(M, N, K, epi == EPI_SWIGLU_BF16, ctx->num_sms);
-    WEDLM_TRY(ensure_gemm_scratch(ctx, gp.ws_floats, gp.counters));
+    g.w_packed = true;
+    const bool dual = W2 != nullptr;
+    GemmPlan gp = plan_gemm_tc(M, N, K, dual, ctx->num_sms);
+    if (ps) {
+      if (gp.slot_floats > m->slot_floats) {
+        WEDLM_CUDA_TRY(cudaStreamSynchronize(st));
+        cudaFree(m->slots);
+        m->slots = nullptr;
+        m->slot_floats = 0;
+        WEDLM_CUDA_TRY(cudaMalloc(&m->slots, gp.slot_floats * sizeof(float)));
+        m->slot_floats = gp.slot_floats;
+      }
+      g.slots = m->slots;
+      *ps = partial_set(gp, m->slots, dual);
+      if (!ctx->dev_err) WEDLM_TRY(ensure_gemm_scratch(ctx, 0, 0));
+    } else {
+      WEDLM_TRY(ensure_gemm_scratch(ctx, gp.ws_floats, gp.counters));
+    }
     const int ph = prof_begin(ctx, st);
     Status s = run_gemm_tc(g, gp, ctx->gemm_ws, ctx->gemm_counters, ctx->dev_err, st);
-    prof_end(ctx, st, ph, WedlmProfiler::kGemm, bytes, flops, gp.grid > 1 ? 2 : 1);
+    prof_end(ctx, st, ph, WedlmProfiler::kGemm, bytes, flops, (!ps && gp.grid > 1) ? 2 : 1);
     return s;
   };
   // algorithmic bytes / flops of the other kernels of one layer
@@ -585,36 +622,76 @@ Status model_forward(wedlm_ctx* ctx, const std::vector<SeqSlice>& seqs, const in
     prof_end(ctx, st, ph, WedlmProfiler::kOther, bytes, 0, 1);
     return s;
   };
-
-  for (int l = 0; l < m->nlayers; ++l) {
-    const LayerWeights& L = m->layers[l];
-    int ph = prof_begin(ctx, st);
-    WEDLM_TRY(other(run_rmsnorm(m->h, H, L.ln1, R, m->H, m->eps, m->dt, m->xn, H, st), ph, norm_bytes));
-    WEDLM_TRY(gemm(m->xn, H, L.wqkv, nullptr, m->qkvdim, m->H, EPI_STORE_BF16, m->qkv, m->qkvdim,
-                   nullptr, 0, R));
-    rk.layer = l;
-    rk.q_norm = L.qn;
-    rk.k_norm = L.kn;
-    ph = prof_begin(ctx, st);
-    WEDLM_TRY(other(run_rope_kv(rk, m->dt, st), ph, rope_bytes));
+  auto attention = [&](int l) -> Status {
     aa.layer = l;
-    ph = prof_begin(ctx, st);
-    if (tc) WEDLM_TRY(run_attention_tc(aa, plan, err, st));
-    else WEDLM_TRY(run_attention_f32(aa, st));
+    const int ph = prof_begin(ctx, st);
+    Status s = tc ? run_attention_tc(aa, plan, err, st) : run_attention_f32(aa, st);
     prof_end(ctx, st, ph, WedlmProfiler::kAttention, attn_bytes, attn_flops,
              tc ? 1 + (plan.n_comb > 0) : 1);
-    WEDLM_TRY(gemm(m->attn, m->qdim, L.wo, nullptr, m->H, m->qdim, EPI_RESID_BF16, m->h, H, m->h,
-                   H, R));
-    ph = prof_begin(ctx, st);
-    WEDLM_TRY(other(run_rmsnorm(m->h, H, L.ln2, R, m->H, m->eps, m->dt, m->xn, H, st), ph, norm_bytes));
-    WEDLM_TRY(gemm(m->xn, H, L.wgate, L.wup, m->I, m->H, EPI_SWIGLU_BF16, m->act, m->I, nullptr, 0,
-                   R));
-    WEDLM_TRY(gemm(m->act, m->I, L.wdown, nullptr, m->H, m->I, EPI_RESID_BF16, m->h, H, m->h, H, R));
+    return s;
+  };
+
+  if (tc) {
+    // bf16: split-K partials are summed by the consuming kernel (RoPE / residual + norm /
+    // SwiGLU); the residual add and the following RMSNorm are one kernel.
+    PartialSet ps;
+    int ph = prof_begin(ctx, st);
+    WEDLM_TRY(other(run_resid_norm(m->h, nullptr, m->layers[0].ln1, R, m->H, m->eps, m->xn, st),
+                    ph, norm_bytes));
+    for (int l = 0; l < m->nlayers; ++l) {
+      const LayerWeights& L = m->layers[l];
+      WEDLM_TRY(gemm(m->xn, H, L.wqkv, nullptr, m->qkvdim, m->H, EPI_STORE_BF16, nullptr, 0,
+                     nullptr, 0, R, &ps));
+      rk.layer = l;
+      rk.q_norm = L.qn;
+      rk.k_norm = L.kn;
+      rk.qkv_partials = &ps;
+      ph = prof_begin(ctx, st);
+      WEDLM_TRY(other(run_rope_kv(rk, m->dt, st), ph, rope_bytes));
+      WEDLM_TRY(attention(l));
+      WEDLM_TRY(gemm(m->attn, m->qdim, L.wo, nullptr, m->H, m->qdim, EPI_STORE_BF16, nullptr, 0,
+                     nullptr, 0, R, &ps));
+      ph = prof_begin(ctx, st);
+      WEDLM_TRY(other(run_resid_norm(m->h, &ps, L.ln2, R, m->H, m->eps, m->xn, st), ph, 2 * norm_bytes));
+      WEDLM_TRY(gemm(m->xn, H, L.wgate, L.wup, m->I, m->H, EPI_SWIGLU_BF16, nullptr, 0, nullptr, 0,
+                     R, &ps));
+      ph = prof_begin(ctx, st);
+      WEDLM_TRY(other(run_swiglu(ps, R, m->I, m->act, st), ph, (double)R * m->I * es));
+      WEDLM_TRY(gemm(m->act, m->I, L.wdown, nullptr, m->H, m->I, EPI_STORE_BF16, nullptr, 0,
+                     nullptr, 0, R, &ps));
+      // residual add + the next RMSNorm: next layer's input norm, or the final norm
+      const float* wn = (l + 1 < m->nlayers) ? m->layers[l + 1].ln1 : m->final_norm;
+      ph = prof_begin(ctx, st);
+      WEDLM_TRY(other(run_resid_norm(m->h, &ps, wn, R, m->H, m->eps, m->xn, st), ph, 2 * norm_bytes));
+    }
+  } else {
+    for (int l = 0; l < m->nlayers; ++l) {
+      const LayerWeights& L = m->layers[l];
+      int ph = prof_begin(ctx, st);
+      WEDLM_TRY(other(run_rmsnorm(m->h, H, L.ln1, R, m->H, m->eps, m->dt, m->xn, H, st), ph, norm_bytes));
+      WEDLM_TRY(gemm(m->xn, H, L.wqkv, nullptr, m->qkvdim, m->H, EPI_STORE_BF16, m->qkv, m->qkvdim,
+                     nullptr, 0, R, nullptr));
+      rk.layer = l;
+      rk.q_norm = L.qn;
+      rk.k_norm = L.kn;
+      rk.qkv_partials = nullptr;
+      ph = prof_begin(ctx, st);
+      WEDLM_TRY(other(run_rope_kv(rk, m->dt, st), ph, rope_bytes));
+      WEDLM_TRY(attention(l));
+      WEDLM_TRY(gemm(m->attn, m->qdim, L.wo, nullptr, m->H, m->qdim, EPI_RESID_BF16, m->h, H, m->h,
+                     H, R, nullptr));
+      ph = prof_begin(ctx, st);
+      WEDLM_TRY(other(run_rmsnorm(m->h, H, L.ln2, R, m->H, m->eps, m->dt, m->xn, H, st), ph, norm_bytes));
+      WEDLM_TRY(gemm(m->xn, H, L.wgate, L.wup, m->I, m->H, EPI_SWIGLU_BF16, m->act, m->I, nullptr, 0,
+                     R, nullptr));
+      WEDLM_TRY(gemm(m->act, m->I, L.wdown, nullptr, m->H, m->I, EPI_RESID_BF16, m->h, H, m->h, H, R,
+                     nullptr));
+    }
   }
   for (int b = 0; b < B; ++b) m->pending_rows[seqs[b].slot] = seqs[b].rows;
   if (!logits || RL == 0) return Status::ok();
 
-  {
+  if (!tc) {
     const int ph = prof_begin(ctx, st);
     Status sn = run_rmsnorm(m->h, H, m->final_norm, R, m->H, m->eps, m->dt, m->xn, H, st);
     prof_end(ctx, st, ph, WedlmProfiler::kOther, norm_bytes, 0, 1);
@@ -634,7 +711,7 @@ Status model_forward(wedlm_ctx* ctx, const std::vector<SeqSlice>& seqs, const in
   }
   const int lepi = (logits_dtype == WEDLM_F32 && m->dt == WEDLM_BF16) ? EPI_STORE_F32 : EPI_STORE_BF16;
   WEDLM_TRY(gemm(xl, H, m->lm_head, nullptr, m->vshard, m->H, lepi, logits, m->vshard, nullptr, 0,
-                 RL));
+                 RL, nullptr));
   (void)es;
   return Status::ok();
 }
@@ -694,6 +771,22 @@ int wedlm_set_weight(wedlm_ctx* ctx, const char* name, const void* host_data, in
     uint16_t* b = reinterpret_cast<uint16_t*>(buf.data());
     for (long i = 0; i < n; ++i) b[i] = wedlm::f32_to_bf16_bits(get(src0 + i));
   }
+  if (w.packed) {
+    // stage the row-major block on the device, then scatter it into the packed tiles
+    void* tmp = nullptr;
+    cudaError_t e = cudaMalloc(&tmp, buf.size());
+    if (e == cudaSuccess) e = cudaMemcpy(tmp, buf.data(), buf.size(), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+      cudaFree(tmp);
+      return ctx->fail(Status::err(WEDLM_ERR_CUDA, cudaGetErrorString(e)));
+    }
+    Status ps = wedlm::pack_weight(tmp, w.cols, w.pack_row0, w.store_rows, w.cols, w.base, 0);
+    e = cudaDeviceSynchronize();
+    cudaFree(tmp);
+    if (!ps.good()) return ctx->fail(ps);
+    if (e != cudaSuccess) return ctx->fail(Status::err(WEDLM_ERR_CUDA, cudaGetErrorString(e)));
+    return WEDLM_OK;
+  }
   cudaError_t e = cudaMemcpy(w.base, buf.data(), buf.size(), cudaMemcpyHostToDevice);
   if (e != cudaSuccess) return ctx->fail(Status::err(WEDLM_ERR_CUDA, cudaGetErrorString(e)));
   return WEDLM_OK;
@@ -710,6 +803,18 @@ int wedlm_get_weight(wedlm_ctx* ctx, const char* name, void* host_out, int64_t n
   if (!host_out || nbytes != need)
     return ctx->fail(Status::err(WEDLM_ERR_INVALID_ARG,
                                  "host buffer must be " + std::to_string(need) + " bytes"));
+  if (w.packed) {
+    void* tmp = nullptr;
+    cudaError_t e = cudaMalloc(&tmp, need);
+    if (e != cudaSuccess) return ctx->fail(Status::err(WEDLM_ERR_OOM, cudaGetErrorString(e)));
+    Status us = wedlm::unpack_weight(w.base, w.pack_row0, w.store_rows, w.cols, tmp, 0);
+    e = cudaDeviceSynchronize();
+    if (us.good() && e == cudaSuccess) e = cudaMemcpy(host_out, tmp, need, cudaMemcpyDeviceToHost);
+    cudaFree(tmp);
+    if (!us.good()) return ctx->fail(us);
+    if (e != cudaSuccess) return ctx->fail(Status::err(WEDLM_ERR_CUDA, cudaGetErrorString(e)));
+    return WEDLM_OK;
+  }
   cudaError_t e = cudaMemcpy(host_out, w.base, need, cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return ctx->fail(Status::err(WEDLM_ERR_CUDA, cudaGetErrorString(e)));
   return WEDLM_OK;
@@ -725,6 +830,10 @@ int wedlm_init_random(wedlm_ctx* ctx, uint64_t seed, float stdv) {
     const long n = w.store_rows * w.cols;
     if (w.is_norm) {
       wedlm::fill_f32_kernel<<<64, 256>>>(reinterpret_cast<float*>(w.base), n, 1.f);
+    } else if (w.packed) {
+      Status is = wedlm::init_normal_packed(w.base, w.pack_row0, w.store_rows, w.cols, seed,
+                                            (uint64_t)w.tensor_id, w.store_row0 * w.cols, stdv, 0);
+      if (!is.good()) return ctx->fail(is);
     } else if (m->dt == WEDLM_BF16) {
       wedlm::init_normal_kernel<__nv_bfloat16><<<1184, 256>>>(
           reinterpret_cast<__nv_bfloat16*>(w.base), n, seed, (uint64_t)w.tensor_id,

@@ -62,6 +62,8 @@ struct ModelState {
   int* d_meta = nullptr;
   int* h_meta = nullptr;
   size_t meta_ints = 0;
+  float* slots = nullptr;  // split-K partial sets of the layer GEMMs (bf16)
+  long slot_floats = 0;
   float* attn_ws = nullptr;
   long attn_ws_floats = 0;
   void* h_attn_staging = nullptr;

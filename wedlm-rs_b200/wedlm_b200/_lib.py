@@ -86,7 +86,8 @@ _PROTOS = {
     "wedlm_decode_end": (C.c_int, [P]),
     # kernel-level entry points (include/wedlm_b200_kernels.h)
     "wedlm_kernel_gemm": (C.c_int, [P, P, C.c_int64, P, P, C.c_int64, C.c_int, C.c_int, C.c_int,
-                                    C.c_int, C.c_int, P, C.c_int64, P, C.c_int64, P]),
+                                    C.c_int, C.c_int, C.c_int, P, C.c_int64, P, C.c_int64, P]),
+    "wedlm_kernel_pack_weight": (C.c_int, [P, P, C.c_int64, C.c_int, C.c_int, P, P]),
     "wedlm_check_device_error": (C.c_int, [P, P]),
     "wedlm_profile_enable": (C.c_int, [P, C.c_int]),
     "wedlm_profile_read": (C.c_int, [P, C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_double),

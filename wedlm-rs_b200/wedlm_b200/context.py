@@ -178,18 +178,32 @@ class Context:
     # ---- kernel-level entry points ------------------------------------------------------
     EPI_STORE, EPI_STORE_F32, EPI_RESIDUAL, EPI_SWIGLU = 0, 1, 2, 3
 
-    def gemm(self, X, W, out, epilogue: int = 0, W2=None, resid=None, stream=None):
-        """``out[m, n] (epilogue)= sum_k X[m, k] W[n, k]`` through ``wedlm_kernel_gemm``."""
+    def gemm(self, X, W, out, epilogue: int = 0, W2=None, resid=None, stream=None, N=None):
+        """``out[m, n] (epilogue)= sum_k X[m, k] W[n, k]`` through ``wedlm_kernel_gemm``.
+        ``W`` is a row-major [N, K] tensor, or a 1-D packed tensor from ``pack_weight``
+        (then pass ``N``)."""
         import torch
         M, K = X.shape
-        N = W.shape[0]
+        packed = W.dim() == 1
+        if not packed:
+            N = W.shape[0]
         dt = BF16 if X.dtype == torch.bfloat16 else F32
-        rc = lib().wedlm_kernel_gemm(self.h, ptr(X), X.stride(0), ptr(W), ptr(W2), W.stride(0),
-                                     M, N, K, dt, epilogue, ptr(out), out.stride(0), ptr(resid),
+        rc = lib().wedlm_kernel_gemm(self.h, ptr(X), X.stride(0), ptr(W), ptr(W2),
+                                     K if packed else W.stride(0), 1 if packed else 0, M, N, K,
+                                     dt, epilogue, ptr(out), out.stride(0), ptr(resid),
                                      resid.stride(0) if resid is not None else 0,
                                      stream_ptr(stream))
         check(rc, self.h)
         return out
+
+    def pack_weight(self, W, stream=None):
+        """Packed GEMM tiles of a row-major bf16 [N, K] weight (1-D tensor)."""
+        import torch
+        N, K = W.shape
+        P = torch.zeros(((N + 127) // 128) * 128 * K, dtype=torch.bfloat16, device=W.device)
+        check(lib().wedlm_kernel_pack_weight(self.h, ptr(W), W.stride(0), N, K, ptr(P),
+                                             stream_ptr(stream)), self.h)
+        return P
 
     def check_device_error(self, stream=None):
         check(lib().wedlm_check_device_error(self.h, stream_ptr(stream)), self.h)
