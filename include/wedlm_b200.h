@@ -172,6 +172,25 @@ WEDLM_API int wedlm_entropy_select(wedlm_ctx* ctx, const void* logits, int dtype
                          const int32_t* caps, float* H, int32_t* argmax, float* maxprob,
                          int32_t* selected, int32_t* n_selected, void* stream);
 
+/* wedlm_entropy_select without device allocation (no counterpart in the reference,
+ * whose selection runs on host vectors).  Same arguments, results and errors as
+ * wedlm_entropy_select; the kernels' scratch lives in a fixed 151,552-byte static
+ * device array instead of context buffers that grow by cudaMalloc after a device-wide
+ * synchronisation.  Limits per call: rows <= 4096, nseq <= 1024 and rows x vocabulary
+ * splits <= 8192 (splits = ceil(4 * SMs / rows) capped at ceil(V / 8192)); larger
+ * calls fail with WEDLM_ERR_INVALID_ARG and launch nothing.  The scratch address is
+ * looked up per device on the first call, so make one call on each device before
+ * any stream capture.  The scratch is shared by every caller in the process on that
+ * device: calls that overlap in time (two streams, or two threads) race on it and
+ * must be serialised by the caller. */
+WEDLM_API int wedlm_entropy_select_noalloc(wedlm_ctx* ctx, const void* logits, int dtype,
+                                           int rows, int V, int ld, float temperature,
+                                           float tau, float lambda, int nseq,
+                                           const int32_t* seq_rows, const int32_t* mask_pos,
+                                           const int32_t* caps, float* H, int32_t* argmax,
+                                           float* maxprob, int32_t* selected,
+                                           int32_t* n_selected, void* stream);
+
 /* Vocab-shard half of the entropy pass: per-row partial softmax statistics over
  * this shard's columns, global column index = vocab_offset + local column.
  * partials: device [rows * 4] f32 words per row: scaled max m, sum exp(x - m),

@@ -68,6 +68,9 @@ _PROTOS = {
     "wedlm_block_forward": (C.c_int, [P, C.c_int, P, P, P, P, C.c_int, P, P, C.c_int, I32P, P]),
     "wedlm_entropy_select": (C.c_int, [P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float,
                                        C.c_float, C.c_float, C.c_int, P, P, P, P, P, P, P, P, P]),
+    "wedlm_entropy_select_noalloc": (C.c_int, [P, P, C.c_int, C.c_int, C.c_int, C.c_int,
+                                               C.c_float, C.c_float, C.c_float, C.c_int, P, P,
+                                               P, P, P, P, P, P, P]),
     "wedlm_entropy_partials": (C.c_int, [P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                          C.c_float, P, P]),
     "wedlm_entropy_combine": (C.c_int, [P, P, C.c_int, C.c_int, C.c_float, C.c_float, C.c_int,

@@ -143,6 +143,23 @@ class Context:
         check(rc, self.h)
         return out
 
+    def entropy_select_noalloc(self, logits, temperature: float, tau: float, lam: float,
+                               seq_rows, mask_pos, caps, out: dict, stream=None) -> dict:
+        """``entropy_select`` through the allocation-free entry point: the caller passes
+        the preallocated outputs ``out`` (keys H, argmax, maxprob, selected,
+        n_selected) and the kernels use a fixed static device scratch."""
+        import torch
+        rows, V = logits.shape[0], logits.shape[1]
+        dt = BF16 if logits.dtype == torch.bfloat16 else F32
+        assert logits.dtype in (torch.bfloat16, torch.float32) and logits.stride(1) == 1
+        nseq = seq_rows.numel() - 1
+        rc = lib().wedlm_entropy_select_noalloc(
+            self.h, ptr(logits), dt, rows, V, logits.stride(0), temperature, tau, lam, nseq,
+            ptr(seq_rows), ptr(mask_pos), ptr(caps), ptr(out["H"]), ptr(out["argmax"]),
+            ptr(out["maxprob"]), ptr(out["selected"]), ptr(out["n_selected"]), stream_ptr(stream))
+        check(rc, self.h)
+        return out
+
     def entropy_partials(self, logits, vocab_offset: int, temperature: float, out=None,
                          stream=None):
         import torch
