@@ -51,12 +51,12 @@ def peaks():
         return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
 
 
-def profile_traffic(name: str):
-    """DRAM bytes per launch recorded by an ncu capture summary under profiles/."""
+def profile_traffic(name: str, key: str = "traffic_bytes_per_launch"):
+    """DRAM bytes recorded by an ncu capture summary under profiles/ (``key:`` line)."""
     p = os.path.join(ROOT, "profiles", name)
     try:
         for line in open(p):
-            if line.startswith("traffic_bytes_per_launch:"):
+            if line.startswith(key + ":"):
                 return float(line.split(":", 1)[1].strip())
     except OSError:
         pass
@@ -260,7 +260,7 @@ def bench_entropy_select(args, rank, ws, local):
         "gpu_launches": args.steps,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / hbm, 4),
-                     "traffic": profile_traffic("entropy_select_c2.md"),
+                     "traffic": profile_traffic("entropy_select_c2.md") if nseq == 64 else None,
                      "kernel": "entropy_select_kernel<bf16>"},
     }
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
@@ -423,7 +423,9 @@ def bench_decode_8b(args, rank, ws, local):
     import torch
     from wedlm_b200 import Context, ModelConfig
     hbm, tflops, peak_kind = peaks()
-    cfg = ModelConfig.wedlm_8b(max_block_tokens=WINDOW_8B)
+    if args.layers != 36 and not args.profile:
+        raise SystemExit("--layers only applies to --profile runs (captures of a reduced model)")
+    cfg = ModelConfig.wedlm_8b(max_block_tokens=WINDOW_8B, num_hidden_layers=args.layers)
     max_ctx = PROMPT_8B + NEW_8B + WINDOW_8B + 64
     ctx = Context(cfg, device=local, max_seqs=1, max_ctx=max_ctx)
     ctx.init_random(seed=0, std=0.02)
@@ -522,7 +524,8 @@ def bench_decode_8b(args, rank, ws, local):
         "roofline": {"bound": "hbm", "achieved": round(gemm_gbs, 1) if gemm_gbs else None,
                      "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s",
                      "frac": round(gemm_gbs / hbm, 4) if gemm_gbs else None,
-                     "traffic": profile_traffic("gemm_tc_decode_8b.md"),
+                     "traffic": profile_traffic("gemm_tc_decode_8b.md", "traffic_bytes_per_step"),
+                     "per": "decode step (all GEMM-class launches of one step)",
                      "kernel": "gemm_tc_kernel (+ shared-tile reduce): QKV/O/gate-up/down/LM head",
                      "launches_per_step": round(g["launches"] / max(args.profile_steps, 1), 1),
                      "share_of_step": round(g["ms"] / max(sum(v["ms"] for v in prof.values()), 1e-9), 3)},
@@ -663,6 +666,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--nseq", type=int, default=64, help="sequences of 96 mask rows per GPU")
     ap.add_argument("--hold-seconds", type=float, default=1.0)
+    ap.add_argument("--layers", type=int, default=36,
+                    help="decoder layers of the decode_8b model (only with --profile: small "
+                         "captures of the same kernels)")
     ap.add_argument("--profile", action="store_true",
                     help="short run for ncu: no load hold, no e2e, no CPU baseline")
     args = ap.parse_args()
