@@ -1,5 +1,6 @@
 // extern "C" entry points of libwedlm_b200.so (declared in include/wedlm_b200.h).
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 
@@ -21,6 +22,14 @@ int set_device(wedlm_ctx* ctx) {
 }  // namespace
 
 namespace wedlm {
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("WEDLM_PDL");
+    return !(e && atoi(e) == 0);
+  }();
+  return on;
+}
 
 Status ensure_entropy_scratch(wedlm_ctx* ctx, int rows, int nseq, long partial_floats) {
   EntropyScratch& W = ctx->ent;

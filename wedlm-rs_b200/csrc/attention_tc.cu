@@ -94,6 +94,8 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int col) {
 __global__ void __launch_bounds__(kThreadsAT, 1)
 attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const AtParams p) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -345,6 +347,8 @@ struct CombineItem {
 };
 
 __global__ void attention_combine_kernel(const CombineItem* items, int nitems, AtParams p) {
+  pdl_trigger();
+  pdl_wait();
   const int wid = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (wid >= nitems * kQT) return;
@@ -495,13 +499,12 @@ Status run_attention_tc(const AttnArgs& a, const AttnPlan& plan, int* err, cudaS
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attr_set |= 1u << dev;
   }
-  attention_tc_kernel<<<(unsigned)plan.n_work, kThreadsAT, smem, st>>>(mQ, mK, mV, p);
-  WEDLM_CUDA_TRY(cudaGetLastError());
+  WEDLM_CUDA_TRY(launch_pdl(attention_tc_kernel, dim3((unsigned)plan.n_work), dim3(kThreadsAT),
+                            smem, st, mQ, mK, mV, p));
   if (plan.n_comb > 0) {
     const long warps = (long)plan.n_comb * kQT;
-    attention_combine_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(
-        reinterpret_cast<const CombineItem*>(plan.comb), plan.n_comb, p);
-    WEDLM_CUDA_TRY(cudaGetLastError());
+    WEDLM_CUDA_TRY(launch_pdl(attention_combine_kernel, dim3((unsigned)((warps + 7) / 8)), dim3(256),
+                              0, st, reinterpret_cast<const CombineItem*>(plan.comb), plan.n_comb, p));
   }
   return Status::ok();
 }

@@ -346,6 +346,8 @@ entropy_select_kernel(const T* __restrict__ logits, int V, long ld, int splits, 
                       const int* __restrict__ caps, float tau, float lambda,
                       float* __restrict__ row_H, float* H, int* argmax, float* maxprob,
                       int* selected, int* n_selected, float* running, const int* running_idx) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x / splits;
   const int split = blockIdx.x - row * splits;
   const int c0 = split * split_cols;
@@ -444,19 +446,14 @@ int pick_splits(int rows, int V, int num_sms) {
 }
 
 template <typename T>
-void launch_select(const EntropyArgs& A, const EntropyScratch& W, int splits, int split_cols,
-                   float invT, bool vec, cudaStream_t st) {
-  dim3 grid((unsigned)(A.rows * splits));
-  if (vec)
-    entropy_select_kernel<T, true><<<grid, kThreads, 0, st>>>(
-        (const T*)A.logits, A.V, A.ld, splits, split_cols, invT, W.partials, W.seq_count, A.nseq,
-        A.seq_rows, A.mask_pos, A.caps, A.tau, A.lambda, W.row_H, A.H, A.argmax, A.maxprob,
-        A.selected, A.n_selected, A.running, A.running_idx);
-  else
-    entropy_select_kernel<T, false><<<grid, kThreads, 0, st>>>(
-        (const T*)A.logits, A.V, A.ld, splits, split_cols, invT, W.partials, W.seq_count, A.nseq,
-        A.seq_rows, A.mask_pos, A.caps, A.tau, A.lambda, W.row_H, A.H, A.argmax, A.maxprob,
-        A.selected, A.n_selected, A.running, A.running_idx);
+cudaError_t launch_select(const EntropyArgs& A, const EntropyScratch& W, int splits,
+                          int split_cols, float invT, bool vec, cudaStream_t st) {
+  const dim3 grid((unsigned)(A.rows * splits));
+  auto kern = vec ? entropy_select_kernel<T, true> : entropy_select_kernel<T, false>;
+  return launch_pdl(kern, grid, dim3(kThreads), 0, st, (const T*)A.logits, A.V, A.ld, splits,
+                    split_cols, invT, W.partials, W.seq_count, A.nseq, A.seq_rows, A.mask_pos,
+                    A.caps, A.tau, A.lambda, W.row_H, A.H, A.argmax, A.maxprob, A.selected,
+                    A.n_selected, A.running, (const int*)A.running_idx);
 }
 
 template <typename T>
@@ -511,10 +508,9 @@ Status run_entropy_select(const EntropyArgs& A, const EntropyScratch& W, int num
   const bool vec = ((uintptr_t)A.logits % 16 == 0) && ((A.ld * dtype_size(A.dtype)) % 16 == 0);
   const float invT = inv_temperature(A.temperature);
   if (A.dtype == WEDLM_BF16)
-    launch_select<__nv_bfloat16>(A, W, p.splits, p.split_cols, invT, vec, st);
+    WEDLM_CUDA_TRY(launch_select<__nv_bfloat16>(A, W, p.splits, p.split_cols, invT, vec, st));
   else
-    launch_select<float>(A, W, p.splits, p.split_cols, invT, vec, st);
-  WEDLM_CUDA_TRY(cudaGetLastError());
+    WEDLM_CUDA_TRY(launch_select<float>(A, W, p.splits, p.split_cols, invT, vec, st));
   return Status::ok();
 }
 

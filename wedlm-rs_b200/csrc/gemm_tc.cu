@@ -189,6 +189,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
   // per-epilogue-warp transpose buffers: [2 accumulators][16 tokens][33]
   float* tbuf = reinterpret_cast<float*>(tail + 1024);
 
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cta = blockIdx.x;
   const long beg = range_start(cta, p.iters, p.grid);
@@ -222,17 +223,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
       const uint64_t pol_w = p.nohint ? policy_evict_last() : policy_evict_first();
       const uint32_t wbytes = (uint32_t)(p.ks * kATileBytes);
       const uint32_t a_bytes = wbytes * (p.dual ? 2 : 1);
-      long issued = 0;
-      for (long it = beg; it < end; ++it) {
-        const long i = it - beg;
-        const int s = (int)(i % p.stages);
-        const uint32_t ph = (uint32_t)(i / p.stages) & 1u;
-        if (!(p.poll ? mbar_spin(empty + s, ph ^ 1u, p.err, kErrWaitEmpty)
-                     : mbar_wait(empty + s, ph ^ 1u, p.err, kErrWaitEmpty)))
-          break;
-        issued = i + 1;
+      // weights of step `it` into ring slot s (arms the slot's full barrier for the stage)
+      auto load_w = [&](long it, int s) {
         const int tile = (int)(it / p.kb_total), kb = (int)(it % p.kb_total) * p.ks;
-        const int n0 = (tile / p.t_tiles) * kTileN, t0 = (tile % p.t_tiles) * p.tok_tile;
+        const int n0 = (tile / p.t_tiles) * kTileN;
         uint8_t* st = smem + s * p.stage_bytes;
         mbar_arrive_expect_tx(full + s, p.stage_bytes);
         if (p.packed) {
@@ -247,8 +241,31 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
               tma_load_2d_hint(st + wbytes + j * kATileBytes, &tmW2, full + s, (kb + j) * kBK, n0, pol_w);
           }
         }
+      };
+      auto load_x = [&](long it, int s) {
+        const int tile = (int)(it / p.kb_total), kb = (int)(it % p.kb_total) * p.ks;
+        const int t0 = (tile % p.t_tiles) * p.tok_tile;
+        uint8_t* st = smem + s * p.stage_bytes;
         for (int j = 0; j < p.ks; ++j)
           tma_load_2d(st + a_bytes + j * p.tok_tile * kBK * 2, &tmX, full + s, (kb + j) * kBK, t0);
+      };
+      // The weights do not depend on the previous kernel: fill every ring slot with them
+      // while that kernel finishes, then wait for it before the first activation load.
+      const long pre = (end - beg) < p.stages ? (end - beg) : p.stages;
+      for (long i = 0; i < pre; ++i) load_w(beg + i, (int)i);
+      pdl_wait();
+      for (long i = 0; i < pre; ++i) load_x(beg + i, (int)i);
+      long issued = pre;
+      for (long it = beg + pre; it < end; ++it) {
+        const long i = it - beg;
+        const int s = (int)(i % p.stages);
+        const uint32_t ph = (uint32_t)(i / p.stages) & 1u;
+        if (!(p.poll ? mbar_spin(empty + s, ph ^ 1u, p.err, kErrWaitEmpty)
+                     : mbar_wait(empty + s, ph ^ 1u, p.err, kErrWaitEmpty)))
+          break;
+        issued = i + 1;
+        load_w(it, s);
+        load_x(it, s);
       }
       // drain: wait for the last load issued to every stage before the CTA may exit
       for (long s = 0; s < p.stages && s < issued; ++s) {
@@ -304,6 +321,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
     }
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
+    pdl_wait();  // outputs may still be read by the previous kernel
     const int q = warp & 3;
     const int na = p.dual ? 2 : 1;
     const long slot_floats = (long)na * p.tok_tile * kTileN;
@@ -380,6 +398,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
 // epilogue.  CTA c (1 <= c < grid) owns the tile holding range boundary start(c) when
 // that boundary is not a tile edge and no smaller boundary falls inside the same tile.
 __global__ void __launch_bounds__(256) gemm_reduce_kernel(const TcParams p) {
+  pdl_trigger();
+  pdl_wait();
   const int c = blockIdx.x + 1;
   const long x = range_start(c, p.iters, p.grid);
   if (x % p.kb_total == 0) return;
@@ -682,12 +702,10 @@ Status run_gemm_tc(const GemmArgs& a, const GemmPlan& g, float* ws, unsigned* co
                                         227 * 1024));
     attr_set |= 1u << dev;
   }
-  gemm_tc_kernel<<<(unsigned)g.grid, kThreadsTC, g.smem_bytes, st>>>(mW, mW2, mX, p);
-  WEDLM_CUDA_TRY(cudaGetLastError());
-  if (g.grid > 1 && !p.slot_mode) {
-    gemm_reduce_kernel<<<(unsigned)(g.grid - 1), 256, 0, st>>>(p);
-    WEDLM_CUDA_TRY(cudaGetLastError());
-  }
+  WEDLM_CUDA_TRY(launch_pdl(gemm_tc_kernel, dim3((unsigned)g.grid), dim3(kThreadsTC),
+                            g.smem_bytes, st, mW, mW2, mX, p));
+  if (g.grid > 1 && !p.slot_mode)
+    WEDLM_CUDA_TRY(launch_pdl(gemm_reduce_kernel, dim3((unsigned)(g.grid - 1)), dim3(256), 0, st, p));
   return Status::ok();
 }
 

@@ -23,6 +23,8 @@ __device__ __forceinline__ T rnd(float v) {
 template <typename T>
 __global__ void embed_kernel(const T* __restrict__ table, const int* __restrict__ ids, int H,
                              T* __restrict__ out, int vocab, int* err) {
+  pdl_trigger();
+  pdl_wait();
   const int r = blockIdx.x;
   int id = ids[r];
   if (id < 0 || id >= vocab) {
@@ -73,6 +75,8 @@ __global__ void rmsnorm_kernel(const T* __restrict__ x, long ldx, const float* _
 // element i (i +/- d/2) sits in lane ^ 16 at the same slot.
 template <typename T, int E>
 __global__ void rope_kv_kernel(RopeKvArgs a, PartialSet ps_val) {
+  pdl_trigger();
+  pdl_wait();
   if (a.qkv_partials != nullptr) a.qkv_partials = &ps_val;
   const int warps = blockDim.x >> 5;
   const int gw = blockIdx.x * warps + (threadIdx.x >> 5);
@@ -207,6 +211,8 @@ __global__ void attention_f32_kernel(AttnArgs a) {
 __global__ void __launch_bounds__(512)
 resid_norm_kernel(__nv_bfloat16* h, PartialSet ps, int has_ps, const float* __restrict__ w,
                   int H, float eps, __nv_bfloat16* xn) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ float srow[];
   const int r = blockIdx.x;
   __nv_bfloat16* hr = h + (long)r * H;
@@ -257,6 +263,8 @@ resid_norm_kernel(__nv_bfloat16* h, PartialSet ps, int has_ps, const float* __re
 
 // ---- SwiGLU from the gate/up partials ---------------------------------------------------
 __global__ void swiglu_kernel(PartialSet ps, int rows, int I, __nv_bfloat16* act) {
+  pdl_trigger();
+  pdl_wait();
   const long n4 = (long)rows * I / 4;
   for (long e4 = blockIdx.x * (long)blockDim.x + threadIdx.x; e4 < n4; e4 += (long)gridDim.x * blockDim.x) {
     const long e = e4 * 4;
@@ -286,9 +294,8 @@ Status run_resid_norm(void* h, const PartialSet* ps, const float* w, int rows, i
   if (rows == 0) return Status::ok();
   WEDLM_CHECK_ARG(H % 4 == 0, "hidden size must be a multiple of 4");
   const PartialSet p = ps ? *ps : PartialSet();
-  resid_norm_kernel<<<rows, 512, (size_t)H * sizeof(float), st>>>(
-      (__nv_bfloat16*)h, p, ps ? 1 : 0, w, H, eps, (__nv_bfloat16*)xn);
-  WEDLM_CUDA_TRY(cudaGetLastError());
+  WEDLM_CUDA_TRY(launch_pdl(resid_norm_kernel, dim3(rows), dim3(512), (size_t)H * sizeof(float), st,
+                            (__nv_bfloat16*)h, p, ps ? 1 : 0, w, H, eps, (__nv_bfloat16*)xn));
   return Status::ok();
 }
 
@@ -297,8 +304,8 @@ Status run_swiglu(const PartialSet& ps, int rows, int I, void* act, cudaStream_t
   WEDLM_CHECK_ARG(I % 4 == 0, "intermediate size must be a multiple of 4");
   const long n4 = (long)rows * I / 4;
   const unsigned grid = (unsigned)std::min<long>((n4 + 255) / 256, 148L * 16);
-  swiglu_kernel<<<grid, 256, 0, st>>>(ps, rows, I, (__nv_bfloat16*)act);
-  WEDLM_CUDA_TRY(cudaGetLastError());
+  WEDLM_CUDA_TRY(launch_pdl(swiglu_kernel, dim3(grid), dim3(256), 0, st, ps, rows, I,
+                            (__nv_bfloat16*)act));
   return Status::ok();
 }
 
@@ -306,11 +313,11 @@ Status run_embed(const void* table, int dtype, const int* ids, int rows, int H, 
                  void* out, int* err, cudaStream_t st) {
   if (rows == 0) return Status::ok();
   if (dtype == WEDLM_BF16)
-    embed_kernel<__nv_bfloat16><<<rows, 128, 0, st>>>((const __nv_bfloat16*)table, ids, H,
-                                                      (__nv_bfloat16*)out, vocab, err);
+    WEDLM_CUDA_TRY(launch_pdl(embed_kernel<__nv_bfloat16>, dim3(rows), dim3(128), 0, st,
+                              (const __nv_bfloat16*)table, ids, H, (__nv_bfloat16*)out, vocab, err));
   else
-    embed_kernel<float><<<rows, 128, 0, st>>>((const float*)table, ids, H, (float*)out, vocab, err);
-  WEDLM_CUDA_TRY(cudaGetLastError());
+    WEDLM_CUDA_TRY(launch_pdl(embed_kernel<float>, dim3(rows), dim3(128), 0, st,
+                              (const float*)table, ids, H, (float*)out, vocab, err));
   return Status::ok();
 }
 
@@ -340,9 +347,11 @@ Status run_rope_kv(const RopeKvArgs& a, int dtype, cudaStream_t st) {
 #define WEDLM_ROPE_CASE(EE)                                                              \
   case EE:                                                                               \
     if (dtype == WEDLM_BF16)                                                             \
-      rope_kv_kernel<__nv_bfloat16, EE><<<grid, per_block * 32, 0, st>>>(a, psv);       \
+      WEDLM_CUDA_TRY(launch_pdl(rope_kv_kernel<__nv_bfloat16, EE>, dim3(grid),          \
+                                dim3(per_block * 32), 0, st, a, psv));                   \
     else                                                                                 \
-      rope_kv_kernel<float, EE><<<grid, per_block * 32, 0, st>>>(a, psv);               \
+      WEDLM_CUDA_TRY(launch_pdl(rope_kv_kernel<float, EE>, dim3(grid), dim3(per_block * 32), \
+                                0, st, a, psv));                                         \
     break;
   switch (E) {
     WEDLM_ROPE_CASE(1)

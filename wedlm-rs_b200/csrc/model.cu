@@ -51,6 +51,8 @@ __global__ void fill_f32_kernel(float* dst, long n, float v) {
 // gather rows src[idx[i]] -> dst[i]
 template <typename T>
 __global__ void gather_rows_kernel(const T* src, long lds, const int* idx, T* dst, long ldd, int H) {
+  pdl_trigger();
+  pdl_wait();
   const int r = blockIdx.x;
   const T* s = src + (long)idx[r] * lds;
   T* dd = dst + (long)r * ldd;
@@ -701,12 +703,13 @@ Status model_forward(wedlm_ctx* ctx, const std::vector<SeqSlice>& seqs, const in
   if (RL != R) {
     ctx->launches += 1;
     if (m->dt == WEDLM_BF16)
-      gather_rows_kernel<__nv_bfloat16><<<RL, 256, 0, st>>>(
-          (const __nv_bfloat16*)m->xn, H, d + o_lsrc, (__nv_bfloat16*)m->xl, H, m->H);
+      WEDLM_CUDA_TRY(launch_pdl(gather_rows_kernel<__nv_bfloat16>, dim3(RL), dim3(256), 0, st,
+                                (const __nv_bfloat16*)m->xn, (long)H, (const int*)(d + o_lsrc),
+                                (__nv_bfloat16*)m->xl, (long)H, m->H));
     else
-      gather_rows_kernel<float><<<RL, 256, 0, st>>>((const float*)m->xn, H, d + o_lsrc,
-                                                    (float*)m->xl, H, m->H);
-    WEDLM_CUDA_TRY(cudaGetLastError());
+      WEDLM_CUDA_TRY(launch_pdl(gather_rows_kernel<float>, dim3(RL), dim3(256), 0, st,
+                                (const float*)m->xn, (long)H, (const int*)(d + o_lsrc),
+                                (float*)m->xl, (long)H, m->H));
     xl = m->xl;
   }
   const int lepi = (logits_dtype == WEDLM_F32 && m->dt == WEDLM_BF16) ? EPI_STORE_F32 : EPI_STORE_BF16;
