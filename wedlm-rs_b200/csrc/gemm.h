@@ -38,6 +38,7 @@ struct PartialSet {
   const float* slots = nullptr;
   long iters = 0;
   int grid = 1, kb_total = 1, t_tiles = 1, tok_tile = 16, maxc = 1, na = 1;
+  int nb = 1;  // weight tiles per stream-K unit
 };
 
 struct GemmArgs {
@@ -58,6 +59,7 @@ struct GemmArgs {
 
 struct GemmPlan {
   int tok_tile = 0, t_tiles = 0, n_tiles = 0, kb_total = 0, splits = 1, stages = 0;
+  int nb = 1;  // weight tiles per stream-K unit (sharing the activation k-blocks)
   int grid = 0, nbuf = 1, maxc = 1;
   int ks = 1, kb64 = 0;  // 64-wide k-blocks per pipeline stage, k-blocks per weight row
   uint32_t stage_bytes = 0, tmem_cols = 0, smem_bytes = 0, acc_cols = 0;
@@ -84,7 +86,7 @@ __device__ __forceinline__ long ps_owner(long x, long iters, int grid) {
 // Sum of the contributors of output (tok, n), accumulator a, in CTA order.
 __device__ __forceinline__ float ps_sum(const PartialSet& p, int tok, int n, int a) {
   const int tile = (n >> 7) * p.t_tiles + tok / p.tok_tile;
-  const long x0 = (long)tile * p.kb_total;
+  const long x0 = (long)(((n >> 7) / p.nb) * p.t_tiles + tok / p.tok_tile) * p.kb_total;
   const int cf = (int)ps_owner(x0, p.iters, p.grid);
   const int cl = (int)ps_owner(x0 + p.kb_total - 1, p.iters, p.grid);
   const float* base = p.slots + ((long)tile * p.maxc * p.na + a) * p.tok_tile * 128 +
@@ -104,7 +106,8 @@ struct PsTile {
 };
 __device__ __forceinline__ PsTile ps_tile(const PartialSet& p, int tok, int n, int a) {
   const int tile = (n >> 7) * p.t_tiles + tok / p.tok_tile;
-  const long x0 = (long)tile * p.kb_total;
+  // first k-step of the stream-K unit holding weight tile n >> 7 (nb tiles per unit)
+  const long x0 = (long)(((n >> 7) / p.nb) * p.t_tiles + tok / p.tok_tile) * p.kb_total;
   const int cf = (int)ps_owner(x0, p.iters, p.grid);
   const int cl = (int)ps_owner(x0 + p.kb_total - 1, p.iters, p.grid);
   PsTile t;

@@ -45,9 +45,10 @@ constexpr int kATileBytes = kTileN * kBK * 2;
 
 struct TcParams {
   int N, M, K;
-  int n_tiles, t_tiles, kb_total;  // kb_total: k-steps per tile (each ks 64-wide k-blocks)
+  int n_tiles, t_tiles, kb_total;  // kb_total: k-steps per unit (each ks 64-wide k-blocks)
   int ks, kb64;                     // k-blocks per step, 64-wide k-blocks per row
-  long iters;          // tiles * kb_total
+  int nb;              // weight tiles per unit: they share every activation k-block
+  long iters;          // units * kb_total; unit u = (weight group u / t_tiles, token tile u % t_tiles)
   int grid;
   int tok_tile;
   int epi, dual;
@@ -57,7 +58,7 @@ struct TcParams {
   int ldo;
   const __nv_bfloat16* resid;
   int ldr;
-  float* ws;           // [grid][2 slots][na][tok_tile][128 weight rows]
+  float* ws;           // [grid][2 slots][nb][na][tok_tile][128 weight rows]
   int* err;
   const uint8_t* wp;   // packed weight tiles (when packed)
   const uint8_t* wp2;
@@ -159,18 +160,56 @@ __device__ __forceinline__ void epilogue_store_vec(const TcParams& p, int tok, i
 
 struct Seg {
   long it0, it1;  // global iteration range of this segment
-  int tile;
-  bool full;      // covers the whole tile
+  int unit;
+  bool full;      // covers the whole unit
 };
 
 __device__ __forceinline__ Seg segment_at(long it, long end, int kb_total) {
   Seg s;
-  s.tile = (int)(it / kb_total);
-  const long tile_end = (long)(s.tile + 1) * kb_total;
+  s.unit = (int)(it / kb_total);
+  const long unit_end = (long)(s.unit + 1) * kb_total;
   s.it0 = it;
-  s.it1 = end < tile_end ? end : tile_end;
-  s.full = (it == (long)s.tile * kb_total) && (s.it1 == tile_end);
+  s.it1 = end < unit_end ? end : unit_end;
+  s.full = (it == (long)s.unit * kb_total) && (s.it1 == unit_end);
   return s;
+}
+
+// Epilogue transpose of one accumulator chunk.  TMEM lane r (weight row rr + r) holds w
+// consecutive tokens (w = 32 or 16); through the warp's [32][33] shared buffer each lane
+// takes 8 consecutive weight rows, (lane % 4) * 8 .. + 7, of the four tokens
+// i * 8 + lane / 4 (i = 0..3), so that four lanes cover one token's 32 rows and the
+// global stores are whole 128-byte (f32) or 64-byte (bf16) runs.  Conflict-free: bank
+// (token + row) % 32 differs across the warp in both phases.
+__device__ __forceinline__ void epi_transpose(uint32_t taddr, int w, float* tb, int lane,
+                                              float (&o)[4][8]) {
+  float v[32];
+  if (w == 32) {
+    tmem_ld32(taddr, v);
+  } else {
+    float h[16];
+    tmem_ld16(taddr, h);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = h[j];
+#pragma unroll
+    for (int j = 16; j < 32; ++j) v[j] = 0.f;
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) tb[j * 33 + lane] = v[j];
+  __syncwarp();
+  const int r0 = (lane & 3) * 8;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int tl = i * 8 + (lane >> 2);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[i][e] = tb[tl * 33 + r0 + e];
+  }
+  __syncwarp();
+}
+
+// weight tiles present in unit u (the last group may hold fewer than nb)
+__device__ __forceinline__ int unit_tiles(const TcParams& p, int u) {
+  const int left = p.n_tiles - (u / p.t_tiles) * p.nb;
+  return left < p.nb ? left : p.nb;
 }
 
 __global__ void __launch_bounds__(kThreadsTC, 1)
@@ -186,7 +225,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
   uint64_t* acc_full = empty + p.stages;   // [2]
   uint64_t* acc_empty = acc_full + 2;      // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
-  // per-epilogue-warp transpose buffers: [2 accumulators][16 tokens][33]
+  // per-epilogue-warp transpose buffers: [32 tokens][33]
   float* tbuf = reinterpret_cast<float*>(tail + 1024);
 
   pdl_trigger();
@@ -221,33 +260,41 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
         if (p.dual) tma_prefetch_desc(&tmW2);
       }
       const uint64_t pol_w = p.nohint ? policy_evict_last() : policy_evict_first();
+      const int na = p.dual ? 2 : 1;
       const uint32_t wbytes = (uint32_t)(p.ks * kATileBytes);
-      const uint32_t a_bytes = wbytes * (p.dual ? 2 : 1);
-      // weights of step `it` into ring slot s (arms the slot's full barrier for the stage)
+      const uint32_t a_bytes = wbytes * na * p.nb;
+      const uint32_t x_bytes = (uint32_t)(p.ks * p.tok_tile * kBK * 2);
+      // weights of step `it` into ring slot s (arms the slot's full barrier for the stage);
+      // stage layout: [tile j][matrix a][ks k-blocks of 16 KB] ... then the activations
       auto load_w = [&](long it, int s) {
-        const int tile = (int)(it / p.kb_total), kb = (int)(it % p.kb_total) * p.ks;
-        const int n0 = (tile / p.t_tiles) * kTileN;
+        const int u = (int)(it / p.kb_total), kb = (int)(it % p.kb_total) * p.ks;
+        const int nv = unit_tiles(p, u);
         uint8_t* st = smem + s * p.stage_bytes;
-        mbar_arrive_expect_tx(full + s, p.stage_bytes);
-        if (p.packed) {
-          // the ks k-blocks of this step are contiguous in the packed layout
-          const long blk = ((long)(tile / p.t_tiles) * p.kb64 + kb) * kATileBytes;
-          bulk_load_hint(st, p.wp + blk, wbytes, full + s, pol_w);
-          if (p.dual) bulk_load_hint(st + wbytes, p.wp2 + blk, wbytes, full + s, pol_w);
-        } else {
-          for (int j = 0; j < p.ks; ++j) {
-            tma_load_2d_hint(st + j * kATileBytes, &tmW, full + s, (kb + j) * kBK, n0, pol_w);
-            if (p.dual)
-              tma_load_2d_hint(st + wbytes + j * kATileBytes, &tmW2, full + s, (kb + j) * kBK, n0, pol_w);
+        mbar_arrive_expect_tx(full + s, (uint32_t)(nv * na) * wbytes + x_bytes);
+        for (int j = 0; j < nv; ++j) {
+          const int nt = (u / p.t_tiles) * p.nb + j;
+          uint8_t* dw = st + (uint32_t)(j * na) * wbytes;
+          if (p.packed) {
+            // the ks k-blocks of this step are contiguous in the packed layout
+            const long blk = ((long)nt * p.kb64 + kb) * kATileBytes;
+            bulk_load_hint(dw, p.wp + blk, wbytes, full + s, pol_w);
+            if (p.dual) bulk_load_hint(dw + wbytes, p.wp2 + blk, wbytes, full + s, pol_w);
+          } else {
+            for (int jb = 0; jb < p.ks; ++jb) {
+              tma_load_2d_hint(dw + jb * kATileBytes, &tmW, full + s, (kb + jb) * kBK, nt * kTileN, pol_w);
+              if (p.dual)
+                tma_load_2d_hint(dw + wbytes + jb * kATileBytes, &tmW2, full + s, (kb + jb) * kBK,
+                                 nt * kTileN, pol_w);
+            }
           }
         }
       };
       auto load_x = [&](long it, int s) {
-        const int tile = (int)(it / p.kb_total), kb = (int)(it % p.kb_total) * p.ks;
-        const int t0 = (tile % p.t_tiles) * p.tok_tile;
-        uint8_t* st = smem + s * p.stage_bytes;
+        const int u = (int)(it / p.kb_total), kb = (int)(it % p.kb_total) * p.ks;
+        const int t0 = (u % p.t_tiles) * p.tok_tile;
+        uint8_t* st = smem + s * p.stage_bytes + a_bytes;
         for (int j = 0; j < p.ks; ++j)
-          tma_load_2d(st + a_bytes + j * p.tok_tile * kBK * 2, &tmX, full + s, (kb + j) * kBK, t0);
+          tma_load_2d(st + j * p.tok_tile * kBK * 2, &tmX, full + s, (kb + j) * kBK, t0);
       };
       // The weights do not depend on the previous kernel: fill every ring slot with them
       // while that kernel finishes, then wait for it before the first activation load.
@@ -277,10 +324,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
       const uint32_t idesc = idesc_bf16_f32(kTileN, p.tok_tile);
+      const int na = p.dual ? 2 : 1;
+      const uint32_t wbytes = (uint32_t)(p.ks * kATileBytes);
+      const uint32_t nmat = (uint32_t)(p.nb * na);
       bool ok = true;
       int nseg = 0;
       for (long it = beg; it < end && ok;) {
         const Seg sg = segment_at(it, end, p.kb_total);
+        const bool two = unit_tiles(p, sg.unit) * na == 2;
         const int buf = nseg % p.nbuf;
         const uint32_t use = (uint32_t)(nseg / p.nbuf);
         // wait until the epilogue has drained this accumulator buffer
@@ -297,8 +348,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
           }
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + s * p.stage_bytes);
-          const uint32_t wbytes = (uint32_t)(p.ks * kATileBytes);
-          const uint32_t sb = sa + wbytes * (p.dual ? 2 : 1);
+          const uint32_t sb = sa + wbytes * nmat;
+          // one or two weight matrices per stage (two tiles, or gate and up): matrix m at
+          // sa + m * wbytes, accumulator columns m * tok_tile; both share the activations
           for (int jb = 0; jb < p.ks; ++jb) {
             const uint32_t ja = sa + jb * kATileBytes, jx = sb + jb * p.tok_tile * kBK * 2;
 #pragma unroll
@@ -306,7 +358,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
               const bool accum = (j != sg.it0) || (jb != 0) || (kk != 0);
               const uint64_t bd = smem_desc_sw128(jx + kk * 32);
               tc_mma_f16(acc, smem_desc_sw128(ja + kk * 32), bd, idesc, accum);
-              if (p.dual)
+              if (two)
                 tc_mma_f16(acc + (uint32_t)p.tok_tile, smem_desc_sw128(ja + wbytes + kk * 32), bd,
                            idesc, accum);
             }
@@ -332,51 +384,50 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
       const uint32_t use = (uint32_t)(nseg / p.nbuf);
       const bool ok = mbar_wait(acc_full + buf, use & 1u, p.err, kErrWaitAccum);
       tc_fence_after();
-      const uint32_t trow = tmem + (uint32_t)(buf * p.acc_cols) + ((uint32_t)(q * 32) << 16);
-      const int n0 = (sg.tile / p.t_tiles) * kTileN, t0 = (sg.tile % p.t_tiles) * p.tok_tile;
+      const int nv = unit_tiles(p, sg.unit);
+      const int t0 = (sg.unit % p.t_tiles) * p.tok_tile;
       const int tok_end = min(p.tok_tile, p.M - t0);
-      // shared tile: publish this CTA's partial in slot 0 (its first segment) or slot 1
-      // (its last), layout [na][tok_tile][128 weight rows] f32; the reduce kernel sums
-      // the contributors of every shared tile.
-      float* part;
-      if (p.slot_mode) {
-        const int rank = cta - owner_cta((long)sg.tile * p.kb_total, p.iters, p.grid);
-        part = p.slots + ((long)sg.tile * p.maxc + rank) * slot_floats;
-      } else {
-        part = p.ws + ((long)cta * 2 + ((sg.it0 == beg) ? 0 : 1)) * slot_floats;
-      }
-      float* tb = tbuf + (warp - 2) * (2 * 16 * 33);
-      const int jt = lane >> 1, hh = (lane & 1) * 16;   // transposed view: token, row half
-      for (int c = 0; c < p.tok_tile; c += 16) {
-        float v[16], v2[16];
-        tmem_ld16(trow + (uint32_t)c, v);
-        if (p.dual) tmem_ld16(trow + (uint32_t)(p.tok_tile + c), v2);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          tb[j * 33 + lane] = v[j];
-          if (p.dual) tb[16 * 33 + j * 33 + lane] = v2[j];
-        }
-        __syncwarp();
-        float o[16], o2[16];
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          o[k] = tb[jt * 33 + hh + k];
-          o2[k] = p.dual ? tb[16 * 33 + jt * 33 + hh + k] : 0.f;
-        }
-        __syncwarp();
-        const int rr = q * 32 + hh;  // first of this lane's 16 weight rows in the tile
-        if (sg.full && !p.slot_mode) {
-          if (ok && c + jt < tok_end) epilogue_store_vec<16>(p, t0 + c + jt, n0 + rr, o, o2);
+      for (int jn = 0; jn < nv; ++jn) {
+        const int nt = (sg.unit / p.t_tiles) * p.nb + jn;
+        const int n0 = nt * kTileN;
+        const uint32_t trow = tmem + (uint32_t)(buf * p.acc_cols + jn * na * p.tok_tile) +
+                              ((uint32_t)(q * 32) << 16);
+        // shared unit: publish this CTA's partial of weight tile nt, layout
+        // [na][tok_tile][128 weight rows] f32.  Slot mode: slot (tile, rank of this CTA among
+        // the unit's contributors), summed by the consumer kernel.  Direct mode: the CTA's
+        // first-segment or last-segment slot, summed by the reduce kernel.
+        float* part;
+        if (p.slot_mode) {
+          const int rank = cta - owner_cta((long)sg.unit * p.kb_total, p.iters, p.grid);
+          const long tile = (long)nt * p.t_tiles + (sg.unit % p.t_tiles);
+          part = p.slots + (tile * p.maxc + rank) * slot_floats;
         } else {
-          float* dst = part + (long)(c + jt) * kTileN + rr;
+          part = p.ws + (((long)cta * 2 + ((sg.it0 == beg) ? 0 : 1)) * p.nb + jn) * slot_floats;
+        }
+        float* tb = tbuf + (warp - 2) * (32 * 33);
+        const int rr = q * 32 + (lane & 3) * 8;  // this lane's first weight row in the tile
+        for (int c = 0; c < p.tok_tile; c += 32) {
+          const int w = min(32, p.tok_tile - c);  // tokens in this chunk (32, or 16 at the end)
+          float o[4][8], o2[4][8];
+          epi_transpose(trow + (uint32_t)c, w, tb, lane, o);
+          if (p.dual) epi_transpose(trow + (uint32_t)(p.tok_tile + c), w, tb, lane, o2);
 #pragma unroll
-          for (int k = 0; k < 16; k += 4)
-            *reinterpret_cast<float4*>(dst + k) = make_float4(o[k], o[k + 1], o[k + 2], o[k + 3]);
-          if (p.dual) {
-            float* dst2 = part + (long)(p.tok_tile + c + jt) * kTileN + rr;
-#pragma unroll
-            for (int k = 0; k < 16; k += 4)
-              *reinterpret_cast<float4*>(dst2 + k) = make_float4(o2[k], o2[k + 1], o2[k + 2], o2[k + 3]);
+          for (int i = 0; i < 4; ++i) {
+            const int tk = c + i * 8 + (lane >> 2);  // token within the tile
+            if (i * 8 + (lane >> 2) >= w) continue;
+            if (sg.full && !p.slot_mode) {
+              if (ok && tk < tok_end) epilogue_store_vec<8>(p, t0 + tk, n0 + rr, o[i], o2[i]);
+            } else {
+              float* dst = part + (long)tk * kTileN + rr;
+              *reinterpret_cast<float4*>(dst) = make_float4(o[i][0], o[i][1], o[i][2], o[i][3]);
+              *reinterpret_cast<float4*>(dst + 4) = make_float4(o[i][4], o[i][5], o[i][6], o[i][7]);
+              if (p.dual) {
+                float* dst2 = part + (long)(p.tok_tile + tk) * kTileN + rr;
+                *reinterpret_cast<float4*>(dst2) = make_float4(o2[i][0], o2[i][1], o2[i][2], o2[i][3]);
+                *reinterpret_cast<float4*>(dst2 + 4) =
+                    make_float4(o2[i][4], o2[i][5], o2[i][6], o2[i][7]);
+              }
+            }
           }
         }
       }
@@ -403,24 +454,28 @@ __global__ void __launch_bounds__(256) gemm_reduce_kernel(const TcParams p) {
   const int c = blockIdx.x + 1;
   const long x = range_start(c, p.iters, p.grid);
   if (x % p.kb_total == 0) return;
-  const int tile = (int)(x / p.kb_total);
-  const long x0 = (long)tile * p.kb_total, x1 = x0 + p.kb_total;
+  const int unit = (int)(x / p.kb_total);
+  const long x0 = (long)unit * p.kb_total, x1 = x0 + p.kb_total;
   if (c > 1) {
     const long xp = range_start(c - 1, p.iters, p.grid);
-    if (xp > x0) return;  // an earlier boundary lies inside this tile
+    if (xp > x0) return;  // an earlier boundary lies inside this unit
   }
   const int cf = owner_cta(x0, p.iters, p.grid);
   const int cl = owner_cta(x1 - 1, p.iters, p.grid);
   const int na = p.dual ? 2 : 1;
   const long slot_floats = (long)na * p.tok_tile * kTileN;
-  const int n0 = (tile / p.t_tiles) * kTileN, t0 = (tile % p.t_tiles) * p.tok_tile;
+  const int nv = unit_tiles(p, unit);
+  const int t0 = (unit % p.t_tiles) * p.tok_tile;
   const int tok_end = min(p.tok_tile, p.M - t0);
-  for (int e = threadIdx.x; e < tok_end * (kTileN / 8); e += blockDim.x) {
-    const int tok = e / (kTileN / 8), r8 = (e % (kTileN / 8)) * 8;
+  const int per_tile = tok_end * (kTileN / 8);
+  for (int e = threadIdx.x; e < nv * per_tile; e += blockDim.x) {
+    const int j = e / per_tile, ee = e - j * per_tile;
+    const int tok = ee / (kTileN / 8), r8 = (ee % (kTileN / 8)) * 8;
+    const int n0 = ((unit / p.t_tiles) * p.nb + j) * kTileN;
     float a[8] = {0, 0, 0, 0, 0, 0, 0, 0}, a2[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int k = cf; k <= cl; ++k) {
       const int sl = range_start(k, p.iters, p.grid) < x0 ? 1 : 0;
-      const float* src = p.ws + ((long)k * 2 + sl) * slot_floats + (long)tok * kTileN + r8;
+      const float* src = p.ws + (((long)k * 2 + sl) * p.nb + j) * slot_floats + (long)tok * kTileN + r8;
 #pragma unroll
       for (int u = 0; u < 8; u += 4) {
         const float4 f = __ldcg(reinterpret_cast<const float4*>(src + u));
@@ -580,7 +635,8 @@ Status init_normal_packed(void* packed, long row_off, long rows, long K, uint64_
 PartialSet partial_set(const GemmPlan& g, const float* slots, bool dual) {
   PartialSet ps;
   ps.slots = slots;
-  ps.iters = (long)g.n_tiles * g.t_tiles * g.kb_total;
+  ps.iters = (long)((g.n_tiles + g.nb - 1) / g.nb) * g.t_tiles * g.kb_total;
+  ps.nb = g.nb;
   ps.grid = g.grid;
   ps.kb_total = g.kb_total;
   ps.t_tiles = g.t_tiles;
@@ -601,36 +657,45 @@ GemmPlan plan_gemm_tc(int M, int N, int K, bool dual, int num_sms) {
   g.tok_tile = tt < 16 ? 16 : tt;
   g.t_tiles = (M + g.tok_tile - 1) / g.tok_tile;
   g.n_tiles = (N + kTileN - 1) / kTileN;
+  // Weight tiles per unit: two tiles share each activation k-block, which halves the
+  // shared memory the activations take per weight byte and so raises the weight bytes in
+  // flight per SM (LM head at 96 rows: 5.8 TB/s instead of 4.2).  Only for wide outputs:
+  // with few units per SM the larger units double the split-K partials of every CTA.
+  // Dual (gate/up) already shares the activations between two matrices, and above 128
+  // token rows the accumulators of two tiles would not double-buffer in TMEM.
+  int nb = (!dual && g.tok_tile <= 128 && (long)g.n_tiles * g.t_tiles >= 4L * num_sms) ? 2 : 1;
+  if (const char* e = getenv("WEDLM_GEMM_NB")) nb = atoi(e) == 1 ? 1 : nb;
+  g.nb = nb;
+  const int na = dual ? 2 : 1;
   // k-blocks per pipeline stage: larger bulk copies per stage stream faster; keep >= 2
-  // stages and enough k-steps per tile for the stream-K split
+  // stages and enough k-steps per unit for the stream-K split
   const int kb64 = K / kBK;
   int ks = 1;
   if (const char* e = getenv("WEDLM_GEMM_KS")) ks = atoi(e);
   else ks = 4;  // largest stage that still leaves two stages in the budget (see below)
   while (ks > 1 && (kb64 % ks != 0)) ks >>= 1;
   if (ks < 1) ks = 1;
-  while (ks > 1 && 2u * ks * (kATileBytes * (dual ? 2 : 1) +
-                              (M > 256 ? 256 : ((M + 15) / 16) * 16) * kBK * 2) > 192u * 1024u)
+  while (ks > 1 && 2u * ks * (kATileBytes * na * nb + g.tok_tile * kBK * 2) > 192u * 1024u)
     ks >>= 1;
   g.ks = ks;
   g.kb64 = kb64;
   g.kb_total = kb64 / ks;
-  const long iters = (long)g.n_tiles * g.t_tiles * g.kb_total;
+  const long iters = (long)((g.n_tiles + nb - 1) / nb) * g.t_tiles * g.kb_total;
   g.grid = (int)(iters < num_sms ? iters : num_sms);
   g.splits = 1;
-  g.stage_bytes = (uint32_t)(ks * (kATileBytes * (dual ? 2 : 1) + g.tok_tile * kBK * 2));
+  g.stage_bytes = (uint32_t)(ks * (kATileBytes * na * nb + g.tok_tile * kBK * 2));
   const uint32_t budget = 192 * 1024;
   int st = (int)(budget / g.stage_bytes);
   g.stages = st > 16 ? 16 : (st < 2 ? 2 : st);
-  g.acc_cols = (uint32_t)(g.tok_tile * (dual ? 2 : 1));
+  g.acc_cols = (uint32_t)(g.tok_tile * na * nb);
   g.nbuf = g.acc_cols * 2 <= 512 ? 2 : 1;
   uint32_t tc = 32;
   while (tc < g.acc_cols * g.nbuf) tc <<= 1;
   g.tmem_cols = tc;
-  // stages | barriers (<= 1 KB) | epilogue transpose buffers (4 warps x 2 x 16 x 33 f32)
-  g.smem_bytes = 1024 + g.stages * g.stage_bytes + 1024 + 4 * 2 * 16 * 33 * 4;
-  g.ws_floats = (long)g.grid * 2 * (dual ? 2 : 1) * g.tok_tile * kTileN;
-  // most CTAs a tile can be shared by: ceil(kb_total / (iters / grid)) + 1
+  // stages | barriers (<= 1 KB) | epilogue transpose buffers (4 warps x 32 x 33 f32)
+  g.smem_bytes = 1024 + g.stages * g.stage_bytes + 1024 + 4 * 32 * 33 * 4;
+  g.ws_floats = (long)g.grid * 2 * nb * na * g.tok_tile * kTileN;
+  // most CTAs a unit can be shared by: ceil(kb_total / (iters / grid)) + 1
   const long per = iters / g.grid;
   g.maxc = (int)((g.kb_total + per - 1) / (per > 0 ? per : 1)) + 1;
   if (g.maxc > g.grid) g.maxc = g.grid;
@@ -667,7 +732,8 @@ Status run_gemm_tc(const GemmArgs& a, const GemmPlan& g, float* ws, unsigned* co
   p.kb_total = g.kb_total;
   p.ks = g.ks;
   p.kb64 = g.kb64;
-  p.iters = (long)g.n_tiles * g.t_tiles * g.kb_total;
+  p.iters = (long)((g.n_tiles + g.nb - 1) / g.nb) * g.t_tiles * g.kb_total;
+  p.nb = g.nb;
   p.grid = g.grid;
   p.tok_tile = g.tok_tile;
   p.epi = a.epi;
