@@ -22,6 +22,17 @@ def wide_bf16_config(layers: int = 2, vocab: int = 16384) -> WeDLMConfig:
                        eos_token_id=vocab - 2, mask_token_id=vocab - 1, dtype="bfloat16")
 
 
+def long_ctx_bf16_config() -> WeDLMConfig:
+    """The 8B attention shape (32/8 heads, head_dim 128) on a narrow 1-layer body (hidden
+    1024, SwiGLU 1024, vocab 2048), bf16: cheap enough for the oracle at a 1000-token
+    prefix, where the tensor-core attention gives each CTA several key chunks."""
+    return WeDLMConfig(vocab_size=2048, hidden_size=1024, num_hidden_layers=1,
+                       num_attention_heads=32, num_key_value_heads=8, head_dim=128,
+                       intermediate_size=1024, max_position_embeddings=4096,
+                       rope_theta=1_000_000.0, rms_norm_eps=1e-6, qk_norm=True,
+                       eos_token_id=2046, mask_token_id=2047, dtype="bfloat16")
+
+
 def to_model_config(cfg: WeDLMConfig, max_block_tokens: int = 128):
     from wedlm_b200 import ModelConfig
     return ModelConfig(vocab_size=cfg.vocab_size, hidden_size=cfg.hidden_size,

@@ -23,7 +23,7 @@ pytestmark = pytest.mark.gpu
 from oracle.decoder import OracleDecoder, compute_block_reorder
 from oracle.model import OracleModel, bf16_bits_to_f32, random_weights
 from oracle.sampler import SamplingParams as OSP, row_stats
-from model_configs import c1_config, to_model_config, wide_bf16_config
+from model_configs import c1_config, long_ctx_bf16_config, to_model_config, wide_bf16_config
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
 
@@ -247,3 +247,42 @@ def test_c1_decode_session_step_by_step(c1):
     ref, rst = ctx.generate_streaming(prompt, 30, 12, params(9.0, 0.01, 3), seq=2)
     assert prompt + ids == ref and st["steps"] == rst["steps"] == steps
     assert h2d > 0 and d2h > 0
+
+
+@pytest.mark.parametrize("P", [700, 1000])
+def test_long_prefix_block_forward(P):
+    """Long committed prefix: the tensor-core attention splits the keys so that its work
+    items run in one wave, which gives each CTA several 128-key chunks (K/V stage reuse,
+    online-softmax rescaling of O).  The 256-row prefill chunks exercise the same at
+    every chunk boundary.  Logits against the bf16 oracle with the tolerances of
+    test_wide_bf16_block_forward."""
+    from wedlm_b200 import Context
+    cfg = long_ctx_bf16_config()
+    w = random_weights(cfg, seed=3, std=0.02)
+    ctx = Context(to_model_config(cfg, max_block_tokens=96), max_seqs=1, max_ctx=1200)
+    try:
+        ctx.load_weights(w)
+        rng = np.random.default_rng(P)
+        S = 96
+        prompt = rng.integers(0, cfg.vocab_size - 2, size=P)
+        ctx.reset_sequence(0)
+        ctx.prefill(0, prompt)
+        window = rng.integers(0, cfg.vocab_size - 2, size=S)
+        masks = np.sort(rng.permutation(S)[:70])
+        window[masks] = cfg.mask_token_id
+        ro = compute_block_reorder(window.tolist(), masks.tolist(), P)
+        lg = ctx.forward_with_positions([0], np.array(ro.reordered_block)[None],
+                                        np.array(ro.positions)[None],
+                                        logits_dtype=torch.float32).cpu().numpy()
+        ctx.check_device_error()
+    finally:
+        ctx.close()
+    om = OracleModel(cfg, w, "bf16")
+    ref, _ = om.forward_with_positions(ro.reordered_block, ro.positions, om.prefill_cache(prompt),
+                                       round_logits=False)
+    of = OracleModel(cfg, w, "f32")
+    exact, _ = of.forward_with_positions(ro.reordered_block, ro.positions,
+                                         of.prefill_cache(prompt), round_logits=False)
+    err = np.abs(lg - ref)
+    assert err.mean() <= 0.015 and err.max() <= 0.1, (err.mean(), err.max())
+    assert err.mean() <= np.abs(ref - exact).mean(), (err.mean(), np.abs(ref - exact).mean())

@@ -154,7 +154,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
       for (int i = 0; i < nchunks; ++i) {
         const int s = i % kStages;
         const uint32_t ph = (uint32_t)(i / kStages) & 1u;
-        if (!mbar_wait(kv_empty + s, ph ^ 1u, p.err, kErrWaitEmpty)) break;
+        if (!mbar_wait(kv_empty + s, ph ^ 1u, p.err, kErrAtKvEmpty)) break;
         issued = i + 1;
         uint8_t* st = sKV + s * 4 * kBlk;
         mbar_arrive_expect_tx(kv_full + s, 4 * kBlk);
@@ -170,10 +170,10 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
           tma_load_2d(st + 2 * kBlk + pg * kBlk, &tmV, kv_full + s, 0, vrow);
         }
       }
-      mbar_wait(q_full, 0, p.err, kErrWaitDrain);
+      mbar_wait(q_full, 0, p.err, kErrAtDrainQ);
       for (int s = 0; s < kStages && s < issued; ++s) {
         const int last = s + ((issued - 1 - s) / kStages) * kStages;
-        mbar_wait(kv_full + s, (uint32_t)(last / kStages) & 1u, p.err, kErrWaitDrain);
+        mbar_wait(kv_full + s, (uint32_t)(last / kStages) & 1u, p.err, kErrAtDrainKv);
       }
     }
   } else if (warp == 1) {
@@ -181,15 +181,15 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
       // ---------------- MMA issuer ----------------
       const uint32_t idesc = idesc_bf16_f32(128, 128);
       const uint32_t aq = smem_u32(sQ), ap = smem_u32(sP);
-      bool ok = mbar_wait(q_full, 0, p.err, kErrWaitFull);
+      bool ok = mbar_wait(q_full, 0, p.err, kErrAtMmaQ);
       for (int i = 0; i < nchunks && ok; ++i) {
         const int s = i % kStages;
-        if (!mbar_wait(kv_full + s, (uint32_t)(i / kStages) & 1u, p.err, kErrWaitFull)) break;
+        if (!mbar_wait(kv_full + s, (uint32_t)(i / kStages) & 1u, p.err, kErrAtMmaKv)) break;
         tc_fence_after();
         const uint32_t bk = smem_u32(sKV + s * 4 * kBlk);
         if (i > 0) {
           // O += P(i-1) . V(i-1)
-          if (!mbar_wait(p_full, (uint32_t)(i - 1) & 1u, p.err, kErrWaitFull)) break;
+          if (!mbar_wait(p_full, (uint32_t)(i - 1) & 1u, p.err, kErrAtMmaP)) break;
           tc_fence_after();
           const int sp = (i - 1) % kStages;
           const uint32_t bv = smem_u32(sKV + sp * 4 * kBlk + 2 * kBlk);
@@ -208,7 +208,8 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
                      smem_desc_sw128(bk + (kk >> 2) * kBlk + (kk & 3) * 32), idesc, kk > 0);
         tc_commit(s_full);
       }
-      if (ok && nchunks > 0 && mbar_wait(p_full, (uint32_t)(nchunks - 1) & 1u, p.err, kErrWaitFull)) {
+      if (ok && nchunks > 0 &&
+          mbar_wait(p_full, (uint32_t)(nchunks - 1) & 1u, p.err, kErrAtMmaPLast)) {
         tc_fence_after();
         const int sp = (nchunks - 1) % kStages;
         const uint32_t bv = smem_u32(sKV + sp * 4 * kBlk + 2 * kBlk);
@@ -233,7 +234,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int i = 0; i < nchunks && ok; ++i) {
-      ok = mbar_wait(s_full, (uint32_t)i & 1u, p.err, kErrWaitAccum);
+      ok = mbar_wait(s_full, (uint32_t)i & 1u, p.err, kErrAtSoftS);
       tc_fence_after();
       const int kbase = (w.c0 + i) * kKC;
       // pass 1: masked row max (scores in log2 units)
@@ -254,7 +255,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
       const float base = mn == -INFINITY ? 0.f : mn;
       float ps = 0.f;
       // PV(i-1) must be complete before P is overwritten and O is rescaled
-      if (i > 0) ok = ok && mbar_wait(o_done, (uint32_t)(i - 1) & 1u, p.err, kErrWaitAccum);
+      if (i > 0) ok = ok && mbar_wait(o_done, (uint32_t)(i - 1) & 1u, p.err, kErrAtSoftO);
       tc_fence_after();
       // pass 2: P = 2^(s - max) as bf16 into the swizzled K-major P tile
 #pragma unroll 1
@@ -282,8 +283,12 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
         *reinterpret_cast<uint4*>(prow + sw128_off(qr, col)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         *reinterpret_cast<uint4*>(prow + sw128_off(qr, col + 8)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
       }
-      if (i > 0 && mn > m && m != -INFINITY) {
-        const float f = fast_exp2(m - mn);
+      // Rescale this row of O when its running max grew.  tcgen05.ld / st are warp-wide
+      // (.sync.aligned), so the whole warp takes the branch when any of its rows needs it;
+      // rows that do not keep the factor 1.
+      const bool grow = i > 0 && mn > m && m != -INFINITY;
+      if (__any_sync(0xffffffffu, grow)) {
+        const float f = grow ? fast_exp2(m - mn) : 1.f;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           float v[16];
@@ -297,11 +302,11 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
       m = mn;
       fence_proxy_async_smem();
       tc_fence_before();
-      named_bar_sync(1, 128);
+      ok = named_bar_and(1, 128, ok);  // the four warps leave the loop together
       if (warp == 2 && lane == 0) mbar_arrive(p_full);
     }
     ok = ok && mbar_wait(o_done, (uint32_t)(nchunks > 0 ? nchunks - 1 : 0) & 1u, p.err,
-                         kErrWaitAccum);
+                         kErrAtSoftOLast);
     tc_fence_after();
     const int r = row0 + r_local;
     const int h = g * p.group + (qi % p.group);
@@ -411,14 +416,16 @@ Status plan_attention_tc(const AttnArgs& a, const int* h_seq_rows, const int* h_
     WEDLM_CHECK_ARG(h_seq_rows[b] <= 4096, "window longer than 4096 rows");
     base += (long)a.nkv * ((h_seq_rows[b] * a.group + kQT - 1) / kQT);
   }
-  const long target = 2L * num_sms;
+  // Split the key range so that all work items run in one wave (one CTA per SM: the
+  // kernel's shared memory holds Q, two K/V stages and P): a second wave would double
+  // the fixed cost per item (TMEM allocation, Q load, first K/V latency, epilogue).
   int part = 0;
   for (int b = 0; b < a.nseq; ++b) {
     const int S = h_seq_rows[b], L = h_cache_len[b];
     if (S == 0) continue;
     const int tiles = (S * a.group + kQT - 1) / kQT;
     const int chunks = (L + S + kKC - 1) / kKC;
-    int splits = base > 0 ? (int)((target + base - 1) / base) : 1;
+    int splits = base > 0 ? (int)(num_sms / base) : 1;
     splits = splits < 1 ? 1 : (splits > chunks ? chunks : splits);
     for (int g = 0; g < a.nkv; ++g)
       for (int t = 0; t < tiles; ++t) {

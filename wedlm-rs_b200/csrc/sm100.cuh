@@ -1,8 +1,9 @@
 // Inline-PTX wrappers for the sm_100a features the kernels use: mbarriers, TMA tile
 // loads, and the tcgen05 tensor-core / tensor-memory instructions.
 //
-// Every wait is bounded: after kWaitLimit polls it records an error code in a global
-// word and returns false, so a kernel that loses a handshake exits instead of hanging.
+// Every wait is bounded: after kWaitNs nanoseconds (or kWaitLimit polls) it records an
+// error code in a global word and returns false, so a kernel that loses a handshake
+// exits instead of hanging.
 #pragma once
 
 #include <cuda.h>
@@ -14,6 +15,7 @@ namespace wedlm {
 namespace sm100 {
 
 constexpr uint32_t kWaitLimit = 1u << 24;
+constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s; every legitimate wait is microseconds
 
 enum ErrCode : int {
   kErrNone = 0,
@@ -22,7 +24,24 @@ enum ErrCode : int {
   kErrWaitAccum = 3,
   kErrWaitAccumEmpty = 4,
   kErrWaitDrain = 5,
+  // attention kernel: 16 + wait site
+  kErrAtKvEmpty = 16,
+  kErrAtDrainQ = 17,
+  kErrAtDrainKv = 18,
+  kErrAtMmaQ = 19,
+  kErrAtMmaKv = 20,
+  kErrAtMmaP = 21,
+  kErrAtMmaPLast = 22,
+  kErrAtSoftS = 23,
+  kErrAtSoftO = 24,
+  kErrAtSoftOLast = 25,
 };
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -69,15 +88,23 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
 }
 // Bounded spin on test_wait (no suspension between polls).
 __device__ __forceinline__ bool mbar_spin(uint64_t* bar, uint32_t parity, int* err, int code) {
-  for (uint32_t i = 0; i < (kWaitLimit << 4); ++i)
+  if (mbar_test_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 0; i < (kWaitLimit << 4); ++i) {
     if (mbar_test_wait(bar, parity)) return true;
+    if ((i & 1023u) == 1023u && global_ns() - t0 > kWaitNs) break;
+  }
   if (err) atomicCAS(err, 0, code);
   return false;
 }
 // Bounded wait for the phase with the given parity to complete.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i)
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63u) == 63u && global_ns() - t0 > kWaitNs) break;
+  }
   if (err) atomicCAS(err, 0, code);
   return false;
 }
@@ -215,6 +242,20 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
 
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+// Named barrier that also ANDs a flag over the participating threads (so that warps
+// which share a loop leave it together after a failed wait).
+__device__ __forceinline__ bool named_bar_and(int id, int nthreads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
 }
 
 }  // namespace sm100
