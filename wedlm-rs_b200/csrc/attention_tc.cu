@@ -237,18 +237,25 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
       ok = mbar_wait(s_full, (uint32_t)i & 1u, p.err, kErrAtSoftS);
       tc_fence_after();
       const int kbase = (w.c0 + i) * kKC;
-      // pass 1: masked row max (scores in log2 units)
+      // the chunk's 128 scores of this query row, in registers after one TMEM wait;
+      // masked keys become -inf (log2 units after the scale)
+      float sv[kKC];
+      tmem_ld128(tS + lane_off, sv);
       float cm = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 8; ++c) {
-        float v[16];
-        tmem_ld16(tS + lane_off + c * 16, v);
+      if (kbase + kKC <= L) {  // chunk inside the committed prefix: every key visible
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int kp = kbase + c * 16 + j;
+        for (int j = 0; j < kKC; ++j) {
+          sv[j] *= p.scale_log2;
+          cm = fmaxf(cm, sv[j]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < kKC; ++j) {
+          const int kp = kbase + j;
           bool vis = kp < L;
           if (!vis && kp < L + S) vis = s_rank[kp - L] <= my_rank;
-          if (vis) cm = fmaxf(cm, v[j] * p.scale_log2);
+          sv[j] = vis ? sv[j] * p.scale_log2 : -INFINITY;
+          cm = fmaxf(cm, sv[j]);
         }
       }
       const float mn = fmaxf(m, cm);
@@ -257,31 +264,20 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
       // PV(i-1) must be complete before P is overwritten and O is rescaled
       if (i > 0) ok = ok && mbar_wait(o_done, (uint32_t)(i - 1) & 1u, p.err, kErrAtSoftO);
       tc_fence_after();
-      // pass 2: P = 2^(s - max) as bf16 into the swizzled K-major P tile
-#pragma unroll 1
-      for (int c = 0; c < 8; ++c) {
-        float v[16];
-        tmem_ld16(tS + lane_off + c * 16, v);
-        uint32_t pk[8];
+      // P = 2^(s - max) as bf16 into the swizzled K-major P tile (2^-inf = 0 for masked keys)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          float e2[2];
+      for (int c = 0; c < kKC / 8; ++c) {
+        uint32_t pk[4];
 #pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int kp = kbase + c * 16 + 2 * j + u;
-            bool vis = kp < L;
-            if (!vis && kp < L + S) vis = s_rank[kp - L] <= my_rank;
-            e2[u] = vis ? fast_exp2(v[2 * j + u] * p.scale_log2 - base) : 0.f;
-          }
-          const __nv_bfloat162 h2 = __floats2bfloat162_rn(e2[0], e2[1]);
+        for (int j = 0; j < 4; ++j) {
+          const __nv_bfloat162 h2 = __floats2bfloat162_rn(fast_exp2(sv[c * 8 + 2 * j] - base),
+                                                          fast_exp2(sv[c * 8 + 2 * j + 1] - base));
           ps += __low2float(h2) + __high2float(h2);
           pk[j] = *reinterpret_cast<const uint32_t*>(&h2);
         }
-        const int key0 = c * 16;
-        const int blk = key0 >> 6, col = key0 & 63;
-        uint8_t* prow = sP + blk * kBlk;
-        *reinterpret_cast<uint4*>(prow + sw128_off(qr, col)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        *reinterpret_cast<uint4*>(prow + sw128_off(qr, col + 8)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        const int key0 = c * 8;
+        *reinterpret_cast<uint4*>(sP + (key0 >> 6) * kBlk + sw128_off(qr, key0 & 63)) =
+            make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
       // Rescale this row of O when its running max grew.  tcgen05.ld / st are warp-wide
       // (.sync.aligned), so the whole warp takes the branch when any of its rows needs it;
@@ -311,26 +307,28 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
     const int r = row0 + r_local;
     const int h = g * p.group + (qi % p.group);
     const float inv = l > 0.f ? 1.f / l : 0.f;
-#pragma unroll 1
-    for (int c = 0; c < 8; ++c) {
-      float v[16];
-      tmem_ld16(tO + lane_off + c * 16, v);
-      if (!(ok && qvalid)) continue;
+    float ov[kD];
+    tmem_ld128(tO + lane_off, ov);
+    if (ok && qvalid) {
       if (w.part < 0) {
-        __nv_bfloat16* dst = p.out + (long)r * p.ld_out + (long)h * kD + c * 16;
-        uint32_t pk[8];
+        __nv_bfloat16* dst = p.out + (long)r * p.ld_out + (long)h * kD;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * j] * inv, v[2 * j + 1] * inv);
-          pk[j] = *reinterpret_cast<const uint32_t*>(&h2);
+        for (int c = 0; c < kD / 8; ++c) {
+          uint32_t pk[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const __nv_bfloat162 h2 =
+                __floats2bfloat162_rn(ov[c * 8 + 2 * j] * inv, ov[c * 8 + 2 * j + 1] * inv);
+            pk[j] = *reinterpret_cast<const uint32_t*>(&h2);
+          }
+          *reinterpret_cast<uint4*>(dst + c * 8) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
-        *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        *reinterpret_cast<uint4*>(dst + 8) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
       } else {
-        float* po = p.part_o + ((long)w.part * kQT + qr) * kD + c * 16;
+        float* po = p.part_o + ((long)w.part * kQT + qr) * kD;
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          *reinterpret_cast<float4*>(po + 4 * j) = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        for (int c = 0; c < kD / 4; ++c)
+          *reinterpret_cast<float4*>(po + 4 * c) =
+              make_float4(ov[4 * c], ov[4 * c + 1], ov[4 * c + 2], ov[4 * c + 3]);
       }
     }
     if (ok && qvalid && w.part >= 0) {
