@@ -405,6 +405,92 @@ def bench_gemm_shapes(args, rank, ws, local):
 
 
 # ----------------------------------------------------------------------------------
+ATT_PREFIXES = (512, 2048, 8192)
+
+
+def attention_flops(L: int, S: int = 96, nh: int = 32) -> float:
+    """QK^T and PV over the visible pairs: every query sees the L cached keys and, causal
+    over explicit positions, S(S+1)/2 window pairs in total."""
+    return 4.0 * nh * 128 * (S * L + S * (S + 1) / 2)
+
+
+def bench_block_attention(args, rank, ws, local):
+    """8B-shape block attention alone (32/8 heads, head_dim 128, 96-row window, N(0,1)
+    inputs, ranks = a seeded permutation of the window positions) at prefixes of 512,
+    2048 and 8192 cached tokens.  Each timed launch is bracketed by CUDA events; a
+    256 MB write between launches flushes L2, so K/V come from HBM every time."""
+    import torch
+    from wedlm_b200 import Context
+    hbm, tflops_peak, peak_kind = peaks()
+    ctx = Context(None, device=local)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+    res = {}
+    for L in ATT_PREFIXES:
+        g = torch.Generator(device="cpu").manual_seed(L + rank)
+        S, nh, nkv = 96, 32, 8
+        q = torch.randn(S, nh, 128, generator=g).to(torch.bfloat16).cuda()
+        k = torch.randn(L + S, nkv, 128, generator=g).to(torch.bfloat16).cuda()
+        v = torch.randn(L + S, nkv, 128, generator=g).to(torch.bfloat16).cuda()
+        rk = (L + torch.randperm(S, generator=g)).to(torch.int32).cuda()
+        ctx.attention_prepare(q, k, v, L, rk, stream=stream)
+        out = torch.empty(S, nh * 128, dtype=torch.bfloat16, device="cuda")
+        for _ in range(args.warmup):
+            ctx.attention_run(out, stream=stream)
+        torch.cuda.synchronize()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+        for e0, e1 in evs:
+            flush.fill_(1.0)
+            e0.record(stream)
+            ctx.attention_run(out, stream=stream)
+            e1.record(stream)
+        torch.cuda.synchronize()
+        ctx.check_device_error()
+        ms = sorted(e0.elapsed_time(e1) for e0, e1 in evs)[len(evs) // 2]
+        ms = max_over_ranks(ms, ws)
+        fl = attention_flops(L)
+        byts = (L + S) * nkv * 128 * 2 * 2 + 2 * S * nh * 128 * 2
+        # end to end: host q/k/v in, prepare (layout copy) + attention, host out back
+        hq, hk, hv = q.cpu().pin_memory(), k.cpu().pin_memory(), v.cpu().pin_memory()
+        hout = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        x0.record(stream)
+        for t_dev, t_host in ((dq, hq), (dk, hk), (dv, hv)):
+            t_dev.copy_(t_host, non_blocking=True)
+        ctx.attention_prepare(dq, dk, dv, L, rk, stream=stream)
+        ctx.attention_run(out, stream=stream)
+        hout.copy_(out, non_blocking=True)
+        x1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = max_over_ranks(x0.elapsed_time(x1), ws)
+        res[L] = {"us": round(ms * 1e3, 2), "TFLOPs": round(fl / (ms * 1e-3) / 1e12, 1),
+                  "GBps": round(byts / (ms * 1e-3) / 1e9, 1),
+                  "frac_tensor": round(fl / (ms * 1e-3) / 1e12 / tflops_peak, 4),
+                  "e2e_TFLOPs": round(fl / (e2e_ms * 1e-3) / 1e12, 3),
+                  "h2d_bytes": int((hq.numel() + hk.numel() + hv.numel()) * 2),
+                  "d2h_bytes": int(hout.numel() * 2)}
+        del q, k, v, dq, dk, dv
+    ctx.close()
+    top = res[ATT_PREFIXES[-1]]
+    return {"metric": METRIC, "value": top["TFLOPs"] * ws, "unit": "TFLOP/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": top["us"] / 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: N(0,1) bf16 q/k/v, ranks = seeded permutation of the window positions",
+            "config": {"workload": "block_attention: 8B-shape GQA (32/8 heads, head_dim 128), "
+                                   "96-row window, causal over explicit positions",
+                       "prefixes": {str(k2): v2 for k2, v2 in res.items()},
+                       "l2": "256 MB written between timed launches", "parallelism": f"dp{ws}"},
+            "e2e": {"value": top["e2e_TFLOPs"] * ws, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": top["h2d_bytes"], "d2h_bytes_per_step": top["d2h_bytes"]},
+            "gpu_launches": args.steps * 2,
+            "roofline": {"bound": "tensor", "achieved": top["TFLOPs"], "peak": tflops_peak,
+                         "peak_kind": peak_kind, "unit": "TFLOP/s", "frac": top["frac_tensor"],
+                         "traffic": None, "kernel": "attention_tc_kernel + attention_combine_kernel"}}
+
+
+# ----------------------------------------------------------------------------------
 PROMPT_8B, NEW_8B, WINDOW_8B = 512, 512, 96
 
 
@@ -656,7 +742,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="decode_8b",
-                    choices=["decode_8b", "entropy_select", "gemm_shapes"])
+                    choices=["decode_8b", "entropy_select", "gemm_shapes", "block_attention"])
     ap.add_argument("--gemm-only", default="", help="comma list of gemm_shapes names")
     ap.add_argument("--profile-steps", type=int, default=10,
                     help="decode steps timed per kernel class after the headline region")
@@ -690,6 +776,8 @@ def main():
         line = bench_decode_8b(args, rank, ws, local)
     elif args.workload == "gemm_shapes":
         line = bench_gemm_shapes(args, rank, ws, local)
+    elif args.workload == "block_attention":
+        line = bench_block_attention(args, rank, ws, local)
     else:
         line = bench_entropy_select(args, rank, ws, local)
     if rank == 0:

@@ -40,6 +40,25 @@ WEDLM_API int wedlm_kernel_gemm(wedlm_ctx* ctx, const void* X, int64_t ldx, cons
 WEDLM_API int wedlm_kernel_pack_weight(wedlm_ctx* ctx, const void* W, int64_t ld, int N, int K,
                                        void* packed, void* stream);
 
+/* Block attention of one S-row window against L cached tokens, the attention of the
+ * decode step on caller buffers: softmax(Q K^T / sqrt(128) + mask) V with GQA
+ * (src/model/attention.rs:188-221), every cached key visible and window key j visible
+ * to window query i iff rank[j] <= rank[i] (rank = window index is the reference's
+ * create_causal_mask, attention.rs:255-279; rank = position is causal over explicit
+ * positions).  Tensor cores, head_dim 128, bf16.
+ *   q     device bf16 [S, nh, 128]         queries after QK-norm and RoPE
+ *   k, v  device bf16 [L + S, nkv, 128]    keys (after RoPE) and values: the L cached
+ *                                          tokens, then the S window tokens
+ *   rank  device int32 [S] or NULL (window index)
+ * prepare copies them into the paged cache layout the model uses, inside the context,
+ * and plans the split-KV work (1 <= S <= 4096, nh % nkv == 0, 128 % (nh / nkv) == 0);
+ * run writes out (device bf16 [S, nh * 128], head h at column h * 128) and can be
+ * repeated on the prepared inputs. */
+WEDLM_API int wedlm_kernel_attention_prepare(wedlm_ctx* ctx, const void* q, const void* k,
+                                             const void* v, int L, int S, int nh, int nkv,
+                                             const int32_t* rank, void* stream);
+WEDLM_API int wedlm_kernel_attention_run(wedlm_ctx* ctx, void* out, void* stream);
+
 /* Synchronises `stream`, then reports (and clears) a device-side wait that gave up
  * inside a kernel since the last check: WEDLM_ERR_TIMEOUT, else WEDLM_OK. */
 WEDLM_API int wedlm_check_device_error(wedlm_ctx* ctx, void* stream);

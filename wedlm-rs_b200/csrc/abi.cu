@@ -199,6 +199,7 @@ void wedlm_destroy(wedlm_ctx* ctx) {
   cudaSetDevice(ctx->device);
   cudaDeviceSynchronize();
   wedlm::session_free(ctx);
+  wedlm::free_attention_kernel_scratch(ctx);
   for (cudaEvent_t e : ctx->prof.ev) cudaEventDestroy(e);
   wedlm::model_destroy(ctx);
   wedlm::free_entropy_scratch(ctx);

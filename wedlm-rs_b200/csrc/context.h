@@ -12,6 +12,7 @@
 namespace wedlm {
 struct ModelState;
 struct DecodeSession;
+struct AttnKernelScratch;
 }
 
 // Optional per-kernel-class timing with CUDA events on the launching stream
@@ -56,6 +57,8 @@ struct wedlm_ctx {
   wedlm::ModelState* model = nullptr;
   // step-wise streaming decode (decode.cu); at most one per context
   wedlm::DecodeSession* session = nullptr;
+  // stand-alone block attention (attention_kernel.cu)
+  wedlm::AttnKernelScratch* att = nullptr;
 
   int fail(const wedlm::Status& s) {
     last_error = s.msg;
@@ -75,6 +78,7 @@ void free_gemm_scratch(wedlm_ctx* ctx);
 // Read and clear the device error word; a non-zero code means a bounded wait gave up.
 Status check_device_error(wedlm_ctx* ctx, cudaStream_t st);
 void session_free(wedlm_ctx* ctx);
+void free_attention_kernel_scratch(wedlm_ctx* ctx);
 // Profiler: mark the start of a launch group; returns a handle (or -1 when off).
 int prof_begin(wedlm_ctx* ctx, cudaStream_t st);
 // End the group started by prof_begin: `nlaunch` kernels of class `cls` that moved

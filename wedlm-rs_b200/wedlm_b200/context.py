@@ -222,6 +222,28 @@ class Context:
                                              stream_ptr(stream)), self.h)
         return P
 
+    def attention_prepare(self, q, k, v, L: int, rank=None, stream=None) -> None:
+        """Stand-alone block attention inputs: ``q`` bf16 CUDA ``[S, nh, 128]``, ``k`` /
+        ``v`` bf16 CUDA ``[L + S, nkv, 128]`` (cached tokens first), ``rank`` int32 CUDA
+        ``[S]`` or None (window index)."""
+        S, nh = q.shape[0], q.shape[1]
+        nkv = k.shape[1]
+        assert q.is_contiguous() and k.is_contiguous() and v.is_contiguous()
+        assert k.shape[0] == L + S and v.shape == k.shape and q.shape[2] == 128
+        self._att_shape = (S, nh)
+        check(lib().wedlm_kernel_attention_prepare(self.h, ptr(q), ptr(k), ptr(v), L, S, nh, nkv,
+                                                   ptr(rank) if rank is not None else None,
+                                                   stream_ptr(stream)), self.h)
+
+    def attention_run(self, out=None, stream=None):
+        """Block attention on the prepared inputs; returns bf16 ``[S, nh * 128]``."""
+        import torch
+        S, nh = self._att_shape
+        if out is None:
+            out = torch.empty(S, nh * 128, dtype=torch.bfloat16, device="cuda")
+        check(lib().wedlm_kernel_attention_run(self.h, ptr(out), stream_ptr(stream)), self.h)
+        return out
+
     def check_device_error(self, stream=None):
         check(lib().wedlm_check_device_error(self.h, stream_ptr(stream)), self.h)
 
