@@ -163,7 +163,105 @@ def make_c2_logits(rows: int, V: int, seed: int):
 
 
 # ----------------------------------------------------------------------------------
+def bench_entropy_sharded(args, rank, ws, local):
+    """Vocabulary-sharded entropy-select over `ws` GPUs: every rank holds the columns
+    [r V/ws, (r+1) V/ws) of the same 64 x 96-row bf16 logits, computes per-row partials
+    (max, sum 2^(x-m), sum 2^(x-m)(x-m), argmax) on its shard, the partials (16 B per row)
+    are all-gathered over NCCL, and every rank combines them and applies the commit rule.
+    Strong scaling: the whole job processes the full logits once per step."""
+    import torch
+    import torch.distributed as dist
+    from wedlm_b200 import Context
+    rows_per_seq, nseq = 96, args.nseq
+    rows, V = rows_per_seq * nseq, V_8B
+    assert V % ws == 0 and (V // ws) % 8 == 0
+    Vr = V // ws
+    ctx = Context(None, device=local)
+    full = make_c2_logits(rows, V, seed=1234)
+    shard = full[:, rank * Vr:(rank + 1) * Vr].contiguous()
+    del full
+    torch.cuda.empty_cache()
+    seq_rows = torch.arange(0, rows + 1, rows_per_seq, dtype=torch.int32, device="cuda")
+    mask_pos = torch.arange(rows, dtype=torch.int32, device="cuda") % rows_per_seq
+    caps = torch.full((nseq,), 8, dtype=torch.int32, device="cuda")
+    part = torch.empty(rows, 4, dtype=torch.float32, device="cuda")
+    gath = torch.empty(ws, rows, 4, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def step(src):
+        ctx.entropy_partials(src, rank * Vr, 0.0, out=part, stream=stream)
+        dist.all_gather_into_tensor(gath, part)
+        return ctx.entropy_combine(gath, 0.8, 0.05, seq_rows, mask_pos, caps, stream=stream)
+
+    hbm, _, peak_kind = peaks()
+    clk = ClockSampler(local)
+    clk.start()
+    for _ in range(args.warmup):
+        step(shard)
+    torch.cuda.synchronize()
+    barrier(ws)
+    t0 = time.time()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step(shard)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(ws)
+    clocks = clk.stop(t0, time.time())
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, ws)
+    total = rows * V * 2
+    # partials kernel alone (this rank's shard), for the roofline
+    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    k0.record(stream)
+    for _ in range(args.steps):
+        ctx.entropy_partials(shard, rank * Vr, 0.0, out=part, stream=stream)
+    k1.record(stream)
+    torch.cuda.synchronize()
+    kms = k0.elapsed_time(k1) / args.steps
+    achieved = rows * Vr * 2 / (kms * 1e-3) / 1e9
+    # end to end: the shard from pinned host memory, results back to the host
+    host = shard.cpu().pin_memory()
+    dev = torch.empty_like(shard)
+    h_out = {k: torch.empty(rows if k != "n_selected" else nseq,
+                            dtype=torch.float32 if k in ("H", "maxprob") else torch.int32,
+                            pin_memory=True) for k in ("H", "argmax", "maxprob", "selected", "n_selected")}
+    barrier(ws)
+    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ne2e = max(3, min(args.steps, 10))
+    x0.record(stream)
+    for _ in range(ne2e):
+        dev.copy_(host, non_blocking=True)
+        out = step(dev)
+        for k in h_out:
+            h_out[k].copy_(out[k], non_blocking=True)
+    x1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(x0.elapsed_time(x1) / ne2e, ws)
+    d2h = sum(t.numel() * t.element_size() for t in h_out.values())
+    ctx.close()
+    return {"metric": METRIC, "value": round(total / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded N(0,2.5^2) bf16 logits + one N(8,1) spike per row",
+            "config": {"workload": f"entropy_select vocab-sharded: {nseq} seqs x 96 mask rows x "
+                                   f"151936 vocab over {ws} GPUs ({Vr} columns each), NCCL "
+                                   "all-gather of 16 B per row, combine + commit rule on every rank",
+                       "rows": rows, "vocab": V, "bytes_per_step_total": total,
+                       "l2": f"inputs larger than L2 ({rows * Vr * 2 / 1e9:.2f} GB per GPU)",
+                       "parallelism": f"vocab{ws}"},
+            "clocks": clocks,
+            "e2e": {"value": round(total / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                    "h2d_bytes_per_step": rows * Vr * 2, "d2h_bytes_per_step": d2h},
+            "gpu_launches": args.steps * 2,
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                         "traffic": None, "kernel": "entropy_partials_kernel<bf16> (per rank)"}}
+
+
 def bench_entropy_select(args, rank, ws, local):
+    if ws > 1 and args.shard == "vocab":
+        return bench_entropy_sharded(args, rank, ws, local)
     import torch
     from wedlm_b200 import Context
     rows_per_seq, nseq = 96, args.nseq
@@ -751,6 +849,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--nseq", type=int, default=64, help="sequences of 96 mask rows per GPU")
+    ap.add_argument("--shard", default="vocab", choices=["vocab", "dp"],
+                    help="entropy_select on N > 1 GPUs: shard the vocabulary (NCCL combine of "
+                         "per-row partials) or run independent batches")
     ap.add_argument("--hold-seconds", type=float, default=1.0)
     ap.add_argument("--layers", type=int, default=36,
                     help="decoder layers of the decode_8b model (only with --profile: small "

@@ -78,6 +78,37 @@ def row_stats(logits: np.ndarray, temperature: float):
     return H, am, maxp
 
 
+def shard_partials(logits_shard: np.ndarray, vocab_offset: int, temperature: float):
+    """Per-row partial softmax statistics of one vocabulary shard (columns
+    ``vocab_offset ..``): max m, S = sum exp(x - m), T = sum exp(x - m) * x, and the
+    shard's last-max argmax as a global column.  The split of ``row_stats`` over
+    shards that the vocab-sharded LM head uses; ``combine_partials`` merges them."""
+    x = scale_logits(logits_shard, temperature).astype(np.float64)
+    m = x.max(axis=-1)
+    e = np.exp(x - m[:, None])
+    S = e.sum(axis=-1)
+    T = (e * x).sum(axis=-1)
+    am = vocab_offset + (x.shape[1] - 1 - np.argmax(x[:, ::-1], axis=-1))
+    return m, S, T, am.astype(np.int64)
+
+
+def combine_partials(parts):
+    """Merge shard partials (list of ``shard_partials`` results, in vocabulary order):
+    m = max m_r, S = sum S_r e^(m_r - m), T = sum T_r e^(m_r - m), H = m + ln S - T / S;
+    the argmax is the largest value, ties to the largest global column; max-prob 1 / S."""
+    m = np.max(np.stack([p[0] for p in parts]), axis=0)
+    S = sum(p[1] * np.exp(p[0] - m) for p in parts)
+    T = sum(p[2] * np.exp(p[0] - m) for p in parts)
+    H = (m + np.log(S) - T / S).astype(np.float32)
+    am = parts[0][3].copy()
+    best = parts[0][0].copy()
+    for p in parts[1:]:
+        take = p[0] >= best  # later shards hold larger columns: ties go to them
+        am = np.where(take, p[3], am)
+        best = np.where(take, p[0], best)
+    return H, am.astype(np.int32), (1.0 / S).astype(np.float32)
+
+
 def greedy_argmax_last(probs_row: np.ndarray) -> int:
     """T = 0 branch of ``sample_from_probs_at_indices`` (``sampler.rs:183-190``)."""
     r = np.asarray(probs_row)
