@@ -108,6 +108,14 @@ WEDLM_API int wedlm_get_config(const wedlm_ctx* ctx, wedlm_config* out);
  * (src/weights.rs:27-46 via src/model/*.rs constructors). */
 WEDLM_API int wedlm_set_weight(wedlm_ctx* ctx, const char* name, const void* host_data, int dtype,
                      const int64_t* shape, int ndim);
+/* Every tensor the model needs from a Hugging Face checkpoint directory:
+ * model.safetensors, or the shards listed by model.safetensors.index.json
+ * ("weight_map"), as load_model_vb / load_sharded_vb / load_safetensors_file
+ * (src/weights.rs:27-46, 59-107, 110-131) read them.  BF16 / F16 / F32 / F64 data are
+ * converted to the model dtype (tensor_from_view, weights.rs:135-210); tensors the model
+ * does not use are skipped.  WEDLM_ERR_NOT_FOUND when neither file exists or a needed
+ * tensor is missing, WEDLM_ERR_IO for a malformed file. */
+WEDLM_API int wedlm_load_weights(wedlm_ctx* ctx, const char* model_dir);
 /* Seeded random init on the device: linear and embedding weights N(0, std^2),
  * norm weights 1.  (No reference counterpart; the reference only loads checkpoints.) */
 WEDLM_API int wedlm_init_random(wedlm_ctx* ctx, uint64_t seed, float std);

@@ -224,6 +224,8 @@ std::vector<std::string> all_weight_names(const ModelState* m) {
 
 }  // namespace
 
+std::vector<std::string> model_weight_names(const ModelState* m) { return all_weight_names(m); }
+
 // ---- create / destroy -------------------------------------------------------------------
 Status model_create(wedlm_ctx* ctx, const wedlm_config& c, int max_seqs, int max_ctx) {
   WEDLM_CHECK_ARG(c.vocab_size > 0 && c.hidden_size > 0 && c.num_hidden_layers > 0, "bad shape");

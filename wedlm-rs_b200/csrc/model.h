@@ -1,6 +1,7 @@
 // Model state: weights, paged KV cache, activation buffers and the forward pass.
 #pragma once
 
+#include <string>
 #include <vector>
 
 #include "context.h"
@@ -72,6 +73,8 @@ struct ModelState {
 };
 
 Status model_create(wedlm_ctx* ctx, const wedlm_config& cfg, int max_seqs, int max_ctx);
+// Checkpoint names of every tensor the model needs (safetensors / Hugging Face naming).
+std::vector<std::string> model_weight_names(const ModelState* m);
 void model_destroy(wedlm_ctx* ctx);
 
 // Forward of a batch of windows.  tokens / positions / rank are host arrays over all

@@ -92,6 +92,7 @@ _PROTOS = {
                                     C.c_int, C.c_int, C.c_int, P, C.c_int64, P, C.c_int64, P]),
     "wedlm_kernel_pack_weight": (C.c_int, [P, P, C.c_int64, C.c_int, C.c_int, P, P]),
     "wedlm_check_device_error": (C.c_int, [P, P]),
+    "wedlm_load_weights": (C.c_int, [P, C.c_char_p]),
     "wedlm_kernel_attention_prepare": (C.c_int, [P, P, P, P, C.c_int, C.c_int, C.c_int,
                                                  C.c_int, P, P]),
     "wedlm_kernel_attention_run": (C.c_int, [P, P, P]),

@@ -248,6 +248,11 @@ class Context:
         check(lib().wedlm_check_device_error(self.h, stream_ptr(stream)), self.h)
 
     # ---- model: weights ---------------------------------------------------------------
+    def load_safetensors(self, model_dir: str) -> None:
+        """All model tensors from ``model_dir`` (model.safetensors, or the shards of
+        model.safetensors.index.json)."""
+        check(lib().wedlm_load_weights(self.h, str(model_dir).encode()), self.h)
+
     def set_weight(self, name: str, array) -> None:
         """Upload one checkpoint tensor (numpy f32 / f16, or uint16 bf16 bit patterns
         with ``bf16=True`` semantics via dtype uint16)."""
