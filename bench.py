@@ -589,6 +589,99 @@ def bench_block_attention(args, rank, ws, local):
 
 
 # ----------------------------------------------------------------------------------
+SERVE_SEQS, SERVE_PROMPT, SERVE_NEW = 64, 4096, 1024
+
+
+def bench_serve_8b(args, rank, ws, local):
+    """Batched serving at the 8B shape: 64 sequences in total, split over the GPUs
+    (data parallel, 64 / N per GPU), each a 4096-token uniform random prompt, then
+    streaming decode with window 96 and the fast preset (tau 1.0, lambda 0.05, cap 6),
+    T 0.  One step = one forward over every live window of the GPU (64 / N x 96 rows) +
+    entropy-select + commit.  `value`: committed tokens per second over K timed steps,
+    summed over GPUs; `e2e`: the same including the prompt prefill from host ids."""
+    import numpy as np
+    import torch
+    from wedlm_b200 import Context, ModelConfig, SamplingParams
+    hbm, tflops, peak_kind = peaks()
+    nloc = args.serve_seqs // ws
+    assert nloc >= 1 and args.serve_seqs % ws == 0
+    cfg = ModelConfig.wedlm_8b(max_block_tokens=WINDOW_8B)
+    max_ctx = SERVE_PROMPT + SERVE_NEW + WINDOW_8B + 64
+    ctx = Context(cfg, device=local, max_seqs=nloc, max_ctx=max_ctx)
+    ctx.init_random(seed=0, std=0.02)
+    prompts = np.stack([make_prompt(SERVE_PROMPT, seed=1000 + rank * nloc + b) for b in range(nloc)])
+    params = SamplingParams.preset("fast", temperature=0.0)
+    stream = torch.cuda.current_stream()
+    barrier(ws)
+    torch.cuda.synchronize()
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record(stream)
+    ctx.decode_begin(list(range(nloc)), prompts, SERVE_NEW, WINDOW_8B, params)
+    p1.record(stream)
+    torch.cuda.synchronize()
+    prefill_ms = max_over_ranks(p0.elapsed_time(p1), ws)
+    ctx.decode_step(args.warmup)
+    tok0 = sum(ctx.decode_result(b)[1]["tokens_generated"] for b in range(nloc))
+    n0, h0, d0 = ctx.decode_io_bytes()
+    launches0 = ctx.launch_count()
+    clk = ClockSampler(local)
+    clk.start()
+    time.sleep(0.2)
+    barrier(ws)
+    torch.cuda.synchronize()
+    t0 = time.time()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        ctx.decode_step(1)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(ws)
+    clocks = clk.stop(t0, time.time())
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, ws)
+    tok1 = sum(ctx.decode_result(b)[1]["tokens_generated"] for b in range(nloc))
+    n1, h1, d1 = ctx.decode_io_bytes()
+    launches = ctx.launch_count() - launches0
+    toks = float(tok1 - tok0)
+    steps_here = args.warmup + args.steps
+    if ws > 1:
+        import torch.distributed as dist
+        t = torch.tensor([toks], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t)
+        toks = float(t.item())
+    value = toks / (ms * args.steps * 1e-3)
+    # prompt prefill + the measured steps, prompts from host ids, ids back to host
+    e2e_s = (prefill_ms + ms * steps_here) * 1e-3
+    e2e_tok = toks * steps_here / args.steps
+    ctx.decode_end()
+    rows = nloc * WINDOW_8B
+    flops = 2.0 * rows * 7.568e9
+    ctx.close()
+    return {"metric": METRIC, "value": round(value, 2), "unit": "committed tok/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: random-init N(0,0.02^2) 8B-shape weights, uniform random prompt ids",
+            "config": {"workload": f"serve_8b: {args.serve_seqs} sequences ({nloc} per GPU), "
+                                   f"{SERVE_PROMPT}-token prompts, window 96, fast preset "
+                                   "(tau 1.0, lambda 0.05, cap 6), T 0",
+                       "rows_per_step_per_gpu": rows, "prefill_ms": round(prefill_ms, 1),
+                       "prefill_tok_s": round(ws * nloc * SERVE_PROMPT / (prefill_ms * 1e-3), 1),
+                       "tokens_per_step": round(toks / args.steps, 2),
+                       "l2": "inputs larger than L2 (15.1 GB of weights per step)",
+                       "parallelism": f"dp{ws}"},
+            "clocks": clocks,
+            "e2e": {"value": round(e2e_tok / e2e_s, 2), "unit": "committed tok/s",
+                    "h2d_bytes_per_step": int((h1 - h0) / max(n1 - n0, 1)),
+                    "d2h_bytes_per_step": int((d1 - d0) / max(n1 - n0, 1)),
+                    "scope": "prompt prefill from host ids + warm-up and timed steps"},
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "tensor", "achieved": round(flops / (ms * 1e-3) / 1e12, 1),
+                         "peak": tflops, "peak_kind": peak_kind, "unit": "TFLOP/s",
+                         "frac": round(flops / (ms * 1e-3) / 1e12 / tflops, 4), "traffic": None,
+                         "kernel": "whole step (GEMM flops 2 x rows x 7.57 G parameters)"}}
+
+
+# ----------------------------------------------------------------------------------
 PROMPT_8B, NEW_8B, WINDOW_8B = 512, 512, 96
 
 
@@ -840,7 +933,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="decode_8b",
-                    choices=["decode_8b", "entropy_select", "gemm_shapes", "block_attention"])
+                    choices=["decode_8b", "entropy_select", "gemm_shapes", "block_attention",
+                             "serve_8b"])
     ap.add_argument("--gemm-only", default="", help="comma list of gemm_shapes names")
     ap.add_argument("--profile-steps", type=int, default=10,
                     help="decode steps timed per kernel class after the headline region")
@@ -849,6 +943,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--nseq", type=int, default=64, help="sequences of 96 mask rows per GPU")
+    ap.add_argument("--serve-seqs", type=int, default=SERVE_SEQS,
+                    help="serve_8b: sequences in total over all GPUs")
     ap.add_argument("--shard", default="vocab", choices=["vocab", "dp"],
                     help="entropy_select on N > 1 GPUs: shard the vocabulary (NCCL combine of "
                          "per-row partials) or run independent batches")
@@ -879,6 +975,8 @@ def main():
         line = bench_gemm_shapes(args, rank, ws, local)
     elif args.workload == "block_attention":
         line = bench_block_attention(args, rank, ws, local)
+    elif args.workload == "serve_8b":
+        line = bench_serve_8b(args, rank, ws, local)
     else:
         line = bench_entropy_select(args, rank, ws, local)
     if rank == 0:
