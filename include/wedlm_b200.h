@@ -245,6 +245,28 @@ WEDLM_API int wedlm_decode_io_bytes(const wedlm_ctx* ctx, int64_t* steps, int64_
                                     int64_t* d2h_bytes);
 WEDLM_API int wedlm_decode_end(wedlm_ctx* ctx);
 
+/* Block mode, the decoder's secondary path.
+ * wedlm_generate_block: WeDLMDecoder::generate_block (src/decoding/wedlm.rs:106-259) on
+ * sequence `seq`, whose cache must hold `prefix` (host, n_prefix ids; it is prefilled
+ * again when the committed length differs): a block of block_size masks is re-forwarded
+ * against the prefix each step (its K/V are not committed) and filled by the
+ * entropy / distance rule with the fixed cap params->max_tokens_per_step, until no mask
+ * is left or an EOS is produced.  out_block (host, block_size ids) may keep masks.
+ * wedlm_commit_block: commit_block_to_cache (wedlm.rs:268-296), the n ids at sequential
+ * positions after the committed length.
+ * wedlm_generate_with_stats: generate_with_stats (wedlm.rs:610-705) with the adaptive
+ * block size and cache refresh; out_ids (host) receives prompt ++ blocks (at most
+ * n_prompt + max_new_tokens ids), *n_out their count.  T must be 0. */
+WEDLM_API int wedlm_generate_block(wedlm_ctx* ctx, int seq, const int32_t* prefix, int n_prefix,
+                                   int block_size, const wedlm_sampling_params* params,
+                                   int32_t* out_block, wedlm_block_stats* stats, void* stream);
+WEDLM_API int wedlm_commit_block(wedlm_ctx* ctx, int seq, const int32_t* block, int n,
+                                 void* stream);
+WEDLM_API int wedlm_generate_with_stats(wedlm_ctx* ctx, int seq, const int32_t* prompt,
+                                        int n_prompt, int max_new_tokens, int block_size,
+                                        const wedlm_sampling_params* params, int32_t* out_ids,
+                                        int32_t* n_out, wedlm_block_stats* stats, void* stream);
+
 /* Batched streaming decode: nseq independent sequences stepped together, one
  * forward per step over all live windows (data-parallel batching of
  * generate_streaming).  prompts: host [nseq, n_prompt]; out_ids: host

@@ -286,3 +286,42 @@ def test_long_prefix_block_forward(P):
     err = np.abs(lg - ref)
     assert err.mean() <= 0.015 and err.max() <= 0.1, (err.mean(), err.max())
     assert err.mean() <= np.abs(ref - exact).mean(), (err.mean(), np.abs(ref - exact).mean())
+
+
+@pytest.mark.parametrize("tau,lam,cap", [(0.8, 0.05, 8), (9.0, 0.01, 3)])
+def test_c1_generate_block_matches_oracle(c1, tau, lam, cap):
+    """Block mode (wedlm.rs:106-259): the block re-forwarded against a fixed prefix."""
+    cfg, w, ctx, om = c1
+    prefix = np.random.default_rng(8).integers(1, 4095, size=32).tolist()
+    ctx.reset_sequence(0)
+    ids, blk, st = ctx.generate_block(prefix, 16, params(tau, lam, cap))
+    dec = OracleDecoder(om, cfg.mask_token_id, cfg.eos_token_id)
+    rids, rblk, rst = dec.generate_block(prefix, 16, OSP(temperature=0.0, entropy_threshold=tau,
+                                                         distance_penalty=lam,
+                                                         max_tokens_per_step=cap))
+    assert blk == rblk and ids == rids
+    assert st["steps"] == rst.steps and st["tokens_generated"] == rst.tokens_generated
+    assert st["high_entropy_count"] == rst.high_entropy_count
+    assert abs(st["avg_entropy"] - rst.avg_entropy) <= 1e-3
+    assert abs(st["max_entropy"] - rst.max_entropy) <= 1e-3
+    # the block K/V were not committed; committing the block extends the cache
+    assert ctx.cache_len(0) == 32
+    ctx.commit_block(blk)
+    assert ctx.cache_len(0) == 48
+
+
+def test_c1_generate_with_stats_matches_oracle(c1):
+    """generate_with_stats (wedlm.rs:610-705): adaptive block size (these random-init
+    rows sit near ln 4096 = 8.3 nats, above the soft threshold) and block commits."""
+    cfg, w, ctx, om = c1
+    prompt = np.random.default_rng(9).integers(1, 4095, size=24).tolist()
+    p = params(9.0, 0.01, 3)
+    ids, st = ctx.generate_with_stats(prompt, 40, 16, p)
+    dec = OracleDecoder(om, cfg.mask_token_id, cfg.eos_token_id)
+    rids, rst = dec.generate_with_stats(prompt, 40, 16, OSP(temperature=0.0, entropy_threshold=9.0,
+                                                            distance_penalty=0.01,
+                                                            max_tokens_per_step=3))
+    assert ids == rids
+    for k in ("steps", "tokens_generated", "block_size_reductions", "cache_refreshes"):
+        assert st[k] == getattr(rst, k), k
+    assert abs(st["avg_entropy"] - rst.avg_entropy) <= 1e-3

@@ -93,6 +93,13 @@ _PROTOS = {
     "wedlm_kernel_pack_weight": (C.c_int, [P, P, C.c_int64, C.c_int, C.c_int, P, P]),
     "wedlm_check_device_error": (C.c_int, [P, P]),
     "wedlm_load_weights": (C.c_int, [P, C.c_char_p]),
+    "wedlm_generate_block": (C.c_int, [P, C.c_int, P, C.c_int, C.c_int,
+                                       C.POINTER(WedlmSamplingParams), P,
+                                       C.POINTER(WedlmBlockStats), P]),
+    "wedlm_commit_block": (C.c_int, [P, C.c_int, P, C.c_int, P]),
+    "wedlm_generate_with_stats": (C.c_int, [P, C.c_int, P, C.c_int, C.c_int, C.c_int,
+                                            C.POINTER(WedlmSamplingParams), P, I32P,
+                                            C.POINTER(WedlmBlockStats), P]),
     "wedlm_kernel_attention_prepare": (C.c_int, [P, P, P, P, C.c_int, C.c_int, C.c_int,
                                                  C.c_int, P, P]),
     "wedlm_kernel_attention_run": (C.c_int, [P, P, P]),

@@ -354,6 +354,42 @@ class Context:
         stats = {f: getattr(st, f) for f, _ in WedlmBlockStats._fields_}
         return list(p) + out[:n.value].tolist(), stats
 
+    def generate_block(self, prefix, block_size: int, params: SamplingParams, seq: int = 0,
+                       stream=None):
+        """``WeDLMDecoder::generate_block``: returns (prefix + block, block, stats)."""
+        import numpy as np
+        p = np.ascontiguousarray(prefix, dtype=np.int32)
+        out = np.zeros(block_size, np.int32)
+        st = WedlmBlockStats()
+        pc = params.to_c()
+        check(lib().wedlm_generate_block(self.h, seq, p.ctypes.data, p.size, block_size,
+                                         C.byref(pc), out.ctypes.data, C.byref(st),
+                                         stream_ptr(stream)), self.h)
+        stats = {f: getattr(st, f) for f, _ in WedlmBlockStats._fields_}
+        return list(p) + out.tolist(), out.tolist(), stats
+
+    def commit_block(self, block, seq: int = 0, stream=None) -> None:
+        """``WeDLMDecoder::commit_block_to_cache``."""
+        import numpy as np
+        b = np.ascontiguousarray(block, dtype=np.int32)
+        check(lib().wedlm_commit_block(self.h, seq, b.ctypes.data, b.size, stream_ptr(stream)),
+              self.h)
+
+    def generate_with_stats(self, prompt, max_new_tokens: int, block_size: int,
+                            params: SamplingParams, seq: int = 0, stream=None):
+        """``WeDLMDecoder::generate_with_stats``: returns (prompt + blocks, stats)."""
+        import numpy as np
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(p.size + max_new_tokens + block_size, np.int32)
+        n = C.c_int32()
+        st = WedlmBlockStats()
+        pc = params.to_c()
+        check(lib().wedlm_generate_with_stats(self.h, seq, p.ctypes.data, p.size, max_new_tokens,
+                                              block_size, C.byref(pc), out.ctypes.data,
+                                              C.byref(n), C.byref(st), stream_ptr(stream)), self.h)
+        stats = {f: getattr(st, f) for f, _ in WedlmBlockStats._fields_}
+        return out[:n.value].tolist(), stats
+
     def generate_streaming_batch(self, prompts, max_new_tokens: int, window_size: int,
                                  params: SamplingParams, stream=None):
         import numpy as np
