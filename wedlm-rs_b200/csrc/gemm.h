@@ -133,5 +133,23 @@ __device__ __forceinline__ float4 ps_sum4(const PsTile& t) {
   }
   return s;
 }
+// Same sum with the loads of up to B contributors issued back to back before any add:
+// slots past the count load contributor 0 again (in bounds, never added), so no load is
+// behind a branch.  Longer contributor lists take ps_sum4.
+template <int B>
+__device__ __forceinline__ float4 ps_sum4_nb(const PsTile& t) {
+  if (t.count > B) return ps_sum4(t);
+  float4 u[B];
+#pragma unroll
+  for (int k = 0; k < B; ++k)
+    u[k] = __ldcg(reinterpret_cast<const float4*>(t.base + (k < t.count ? k : 0) * t.stride));
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int k = 0; k < B; ++k)
+    if (k < t.count) {
+      s.x += u[k].x; s.y += u[k].y; s.z += u[k].z; s.w += u[k].w;
+    }
+  return s;
+}
 
 }  // namespace wedlm

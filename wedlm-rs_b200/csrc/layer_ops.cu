@@ -92,7 +92,7 @@ __global__ void rope_kv_kernel(RopeKvArgs a, PartialSet ps_val) {
 #pragma unroll
       for (int e = 0; e < E; e += 4) {
         const PsTile t = ps_tile(*a.qkv_partials, r, hh * d + lane * E + e, 0);
-        const float4 v = ps_sum4(t);
+        const float4 v = ps_sum4_nb<8>(t);
         x[e] = to_f32(rnd<T>(v.x));
         x[e + 1] = to_f32(rnd<T>(v.y));
         x[e + 2] = to_f32(rnd<T>(v.z));
@@ -217,28 +217,46 @@ resid_norm_kernel(__nv_bfloat16* h, PartialSet ps, int has_ps, const float* __re
   const int r = blockIdx.x;
   __nv_bfloat16* hr = h + (long)r * H;
   float ss = 0.f;
-  for (int i = threadIdx.x * 4; i < H; i += blockDim.x * 4) {
-    const uint2 hw = *reinterpret_cast<const uint2*>(hr + i);
-    float v[4] = {bf16_lo(hw.x), bf16_hi(hw.x), bf16_lo(hw.y), bf16_hi(hw.y)};
+  // two float4 groups per iteration, every load of both issued before the arithmetic
+  const int step = blockDim.x * 4;
+  for (int i0 = threadIdx.x * 4; i0 < H; i0 += 2 * step) {
+    const int i1 = i0 + step;
+    const bool two = i1 < H;
+    const uint2 hw0 = *reinterpret_cast<const uint2*>(hr + i0);
+    const uint2 hw1 = two ? *reinterpret_cast<const uint2*>(hr + i1) : hw0;
+    float4 y0 = make_float4(0.f, 0.f, 0.f, 0.f), y1 = y0;
     if (has_ps) {
-      const float4 y = ps_sum4(ps_tile(ps, r, i, 0));
-      const float ys[4] = {y.x, y.y, y.z, y.w};
-      uint32_t o[2];
-#pragma unroll
-      for (int k = 0; k < 4; k += 2) {
-        const float a0 = __bfloat162float(__float2bfloat16_rn(v[k] + __bfloat162float(__float2bfloat16_rn(ys[k]))));
-        const float a1 = __bfloat162float(__float2bfloat16_rn(v[k + 1] + __bfloat162float(__float2bfloat16_rn(ys[k + 1]))));
-        v[k] = a0;
-        v[k + 1] = a1;
-        const __nv_bfloat162 h2 = __floats2bfloat162_rn(a0, a1);
-        o[k / 2] = *reinterpret_cast<const uint32_t*>(&h2);
-      }
-      *reinterpret_cast<uint2*>(hr + i) = make_uint2(o[0], o[1]);
+      const PsTile t0 = ps_tile(ps, r, i0, 0);
+      const PsTile t1 = ps_tile(ps, r, two ? i1 : i0, 0);
+      y0 = ps_sum4_nb<8>(t0);
+      y1 = ps_sum4_nb<8>(t1);
     }
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      srow[i + k] = v[k];
-      ss = fmaf(v[k], v[k], ss);
+    for (int g = 0; g < 2; ++g) {
+      if (g == 1 && !two) break;
+      const int i = g ? i1 : i0;
+      const uint2 hw = g ? hw1 : hw0;
+      const float4 y = g ? y1 : y0;
+      float v[4] = {bf16_lo(hw.x), bf16_hi(hw.x), bf16_lo(hw.y), bf16_hi(hw.y)};
+      if (has_ps) {
+        const float ys[4] = {y.x, y.y, y.z, y.w};
+        uint32_t o[2];
+#pragma unroll
+        for (int k = 0; k < 4; k += 2) {
+          const float a0 = __bfloat162float(__float2bfloat16_rn(v[k] + __bfloat162float(__float2bfloat16_rn(ys[k]))));
+          const float a1 = __bfloat162float(__float2bfloat16_rn(v[k + 1] + __bfloat162float(__float2bfloat16_rn(ys[k + 1]))));
+          v[k] = a0;
+          v[k + 1] = a1;
+          const __nv_bfloat162 h2 = __floats2bfloat162_rn(a0, a1);
+          o[k / 2] = *reinterpret_cast<const uint32_t*>(&h2);
+        }
+        *reinterpret_cast<uint2*>(hr + i) = make_uint2(o[0], o[1]);
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        srow[i + k] = v[k];
+        ss = fmaf(v[k], v[k], ss);
+      }
     }
   }
   __shared__ float sh[32];
@@ -269,8 +287,9 @@ __global__ void swiglu_kernel(PartialSet ps, int rows, int I, __nv_bfloat16* act
   for (long e4 = blockIdx.x * (long)blockDim.x + threadIdx.x; e4 < n4; e4 += (long)gridDim.x * blockDim.x) {
     const long e = e4 * 4;
     const int r = (int)(e / I), j = (int)(e % I);
-    const float4 g4 = ps_sum4(ps_tile(ps, r, j, 0));
-    const float4 u4 = ps_sum4(ps_tile(ps, r, j, 1));
+    const PsTile tg = ps_tile(ps, r, j, 0), tu = ps_tile(ps, r, j, 1);
+    const float4 g4 = ps_sum4_nb<4>(tg);
+    const float4 u4 = ps_sum4_nb<4>(tu);
     const float gs[4] = {g4.x, g4.y, g4.z, g4.w}, us[4] = {u4.x, u4.y, u4.z, u4.w};
     float y[4];
 #pragma unroll
