@@ -182,7 +182,7 @@ WEDLM_API int wedlm_entropy_select(wedlm_ctx* ctx, const void* logits, int dtype
 
 /* wedlm_entropy_select without device allocation (no counterpart in the reference,
  * whose selection runs on host vectors).  Same arguments, results and errors as
- * wedlm_entropy_select; the kernels' scratch lives in a fixed 151,552-byte static
+ * wedlm_entropy_select; the kernels' scratch lives in a fixed 167,936-byte static
  * device array instead of context buffers that grow by cudaMalloc after a device-wide
  * synchronisation.  Limits per call: rows <= 4096, nseq <= 1024 and rows x vocabulary
  * splits <= 8192 (splits = ceil(4 * SMs / rows) capped at ceil(V / 8192)); larger

@@ -23,17 +23,20 @@ constexpr int kNoAllocMaxRowSplits = 8192;   // rows x vocabulary splits per cal
 constexpr int kMaxDevices = 64;
 
 // Layout (bytes): partials [kNoAllocMaxRowSplits][4] f32 | row_H [kNoAllocMaxRows] f32 |
-// seq_count [kNoAllocMaxSeqs] u32.  Total 151,552 bytes.
+// row_count [kNoAllocMaxRows] u32 | seq_count [kNoAllocMaxSeqs] u32.  Total 167,936 bytes.
 constexpr size_t kPartialsOff = 0;
 constexpr size_t kRowHOff = kPartialsOff + sizeof(float) * 4 * kNoAllocMaxRowSplits;
-constexpr size_t kSeqCountOff = kRowHOff + sizeof(float) * kNoAllocMaxRows;
+constexpr size_t kRowCountOff = kRowHOff + sizeof(float) * kNoAllocMaxRows;
+constexpr size_t kSeqCountOff = kRowCountOff + sizeof(unsigned) * kNoAllocMaxRows;
 constexpr size_t kScratchBytes = kSeqCountOff + sizeof(unsigned) * kNoAllocMaxSeqs;
-static_assert(kRowHOff % 256 == 0 && kSeqCountOff % 256 == 0, "scratch sections stay aligned");
+static_assert(kRowHOff % 256 == 0 && kRowCountOff % 256 == 0 && kSeqCountOff % 256 == 0,
+              "scratch sections stay aligned");
+static_assert(kScratchBytes == 167936, "documented size");
 
-// Static storage is zero when the module is loaded.  The seq_count section must be zero
-// before every launch: each launch's last CTA of a sequence puts that sequence's counter
-// back to zero, so the invariant holds from one call to the next.  The other sections
-// are written before they are read within a launch.
+// Static storage is zero when the module is loaded.  The row_count and seq_count sections
+// must be zero before every launch: each launch's last CTA of a row (of a sequence) puts
+// that counter back to zero, so the invariant holds from one call to the next.  The other
+// sections are written before they are read within a launch.
 static __device__ __align__(256) unsigned char g_entropy_scratch[kScratchBytes];
 
 std::atomic<unsigned char*> g_scratch_addr[kMaxDevices];
@@ -91,6 +94,7 @@ extern "C" int wedlm_entropy_select_noalloc(wedlm_ctx* ctx, const void* logits, 
   W.partial_capacity = 4L * kNoAllocMaxRowSplits;
   W.row_H = reinterpret_cast<float*>(base + kRowHOff);
   W.row_capacity = kNoAllocMaxRows;
+  W.row_count = reinterpret_cast<unsigned*>(base + kRowCountOff);
   W.seq_count = reinterpret_cast<unsigned*>(base + kSeqCountOff);
   W.seq_capacity = kNoAllocMaxSeqs;
 

@@ -191,6 +191,11 @@ __device__ __forceinline__ Acc load_partial(const float* p) {
   return a;
 }
 
+__device__ void commit_rule(int b, int r0, int r1, float tau, float lambda,
+                            const int* __restrict__ mask_pos, const int* __restrict__ caps,
+                            const float* row_H, int* selected, int* n_selected, float* running,
+                            const int* running_idx);
+
 // Combine partials of every row of sequence [r0, r1) (partial (r, k) at
 // part + (r * rs + k * ks) * 4), write per-row results, then the commit rule.
 // Runs on one whole CTA of kThreads threads.
@@ -200,7 +205,6 @@ __device__ void finalize_sequence(int b, int r0, int r1, const float* part, long
                                   int* argmax, float* maxprob, int* selected, int* n_selected,
                                   float* running, const int* running_idx) {
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  const int M = r1 - r0;
   for (int r = r0 + w; r < r1; r += kThreads / 32) {
     Acc st;
     acc_init(st);
@@ -219,14 +223,39 @@ __device__ void finalize_sequence(int b, int r0, int r1, const float* part, long
   }
   __syncthreads();
   __threadfence_block();
+  commit_rule(b, r0, r1, tau, lambda, mask_pos, caps, row_H, selected, n_selected, running,
+              running_idx);
+}
 
-  // ---- commit rule: select_by_entropy_with_distance (sampler.rs:446-493) ----
+// The commit rule of sequence b over its rows' entropies row_H[r0 .. r1): entropy EMA and
+// dynamic cap, then select_by_entropy_with_distance (sampler.rs:446-493).  One whole CTA.
+// The positions and entropies are staged in shared memory (sequences up to kRuleRows
+// rows; longer ones read them from global memory).
+constexpr int kRuleRows = 1024;
+__device__ void commit_rule(int b, int r0, int r1, float tau, float lambda,
+                            const int* __restrict__ mask_pos, const int* __restrict__ caps,
+                            const float* row_H, int* selected, int* n_selected, float* running,
+                            const int* running_idx) {
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  const int M = r1 - r0;
+  __shared__ int s_pos[kRuleRows];
+  __shared__ float s_adj[kRuleRows];
+  __shared__ float s_h[kRuleRows];
+  const bool staged = M <= kRuleRows;
+  if (staged)
+    for (int i = threadIdx.x; i < M; i += kThreads) {
+      s_pos[i] = mask_pos[r0 + i];
+      s_h[i] = __ldcg(row_H + r0 + i);
+    }
+  __syncthreads();
+  auto pos_of = [&](int i) { return staged ? s_pos[i] : mask_pos[r0 + i]; };
+  auto h_of = [&](int i) { return staged ? s_h[i] : __ldcg(row_H + r0 + i); };
   __shared__ int sh_i[kThreads / 32];
   __shared__ float sh_f[kThreads / 32];
   __shared__ int sh_r[kThreads / 32];
   // leftmost = min logical position
   int mn = INT_MAX;
-  for (int i = threadIdx.x; i < M; i += kThreads) mn = min(mn, mask_pos[r0 + i]);
+  for (int i = threadIdx.x; i < M; i += kThreads) mn = min(mn, pos_of(i));
   mn = warp_min_i(mn);
   if (l == 0) sh_i[w] = mn;
   __syncthreads();
@@ -244,7 +273,7 @@ __device__ void finalize_sequence(int b, int r0, int r1, const float* part, long
       // entropy EMA and dynamic cap, f32 in the reference's operation order
       // (wedlm.rs:517-535): sequential sum, mean, 0.3 * mean + (1 - 0.3) * r
       float sum = 0.f;
-      for (int i = 0; i < M; ++i) sum = __fadd_rn(sum, __ldcg(row_H + r0 + i));
+      for (int i = 0; i < M; ++i) sum = __fadd_rn(sum, h_of(i));
       const float mean = __fdiv_rn(sum, (float)M);
       const float a = 0.3f;
       const int ri = running_idx ? running_idx[b] : b;
@@ -255,25 +284,39 @@ __device__ void finalize_sequence(int b, int r0, int r1, const float* part, long
     }
     sh_cap = cap0;
   }
+  if (staged)
+    for (int i = threadIdx.x; i < M; i += kThreads)
+      s_adj[i] = __fadd_rn(s_h[i], __fmul_rn(lambda, (float)(s_pos[i] - leftmost)));
   __syncthreads();
   const int cap = sh_cap;
   int npass = 0;
   float best_adj = FLT_MAX;
   int best_rank = INT_MAX, best_i = -1;
   for (int i = threadIdx.x; i < M; i += kThreads) {
-    const int pi = mask_pos[r0 + i];
-    const float hi = __ldcg(row_H + r0 + i);
-    const float adj_i = __fadd_rn(hi, __fmul_rn(lambda, (float)(pi - leftmost)));
+    const int pi = pos_of(i);
+    const float adj_i =
+        staged ? s_adj[i] : __fadd_rn(h_of(i), __fmul_rn(lambda, (float)(pi - leftmost)));
     const bool pass_i = adj_i < tau;
+    // rank of row i in (logical position, row) order, and how many passing rows precede it
     int rank = 0, before = 0;
-    for (int j = 0; j < M; ++j) {
-      const int pj = mask_pos[r0 + j];
-      const bool earlier = pj < pi || (pj == pi && j < i);
-      if (earlier) {
-        ++rank;
-        const float hj = __ldcg(row_H + r0 + j);
-        const float adj_j = __fadd_rn(hj, __fmul_rn(lambda, (float)(pj - leftmost)));
-        before += (adj_j < tau);
+    if (staged) {
+      // branch-free over shared memory
+#pragma unroll 4
+      for (int j = 0; j < M; ++j) {
+        const int pj = s_pos[j];
+        const int earlier = (pj < pi) | ((pj == pi) & (j < i));
+        rank += earlier;
+        before += earlier & (s_adj[j] < tau);
+      }
+    } else {
+      for (int j = 0; j < M; ++j) {
+        const int pj = mask_pos[r0 + j];
+        const bool earlier = pj < pi || (pj == pi && j < i);
+        if (earlier) {
+          ++rank;
+          const float adj_j = __fadd_rn(__ldcg(row_H + r0 + j), __fmul_rn(lambda, (float)(pj - leftmost)));
+          before += (adj_j < tau);
+        }
       }
     }
     if (pass_i) {
@@ -341,8 +384,8 @@ __device__ __forceinline__ int find_seq(const int* __restrict__ seq_rows, int ns
 template <typename T, bool kVec>
 __global__ void __launch_bounds__(kThreads)
 entropy_select_kernel(const T* __restrict__ logits, int V, long ld, int splits, int split_cols,
-                      float invT, float* __restrict__ part, unsigned* __restrict__ seq_count,
-                      int nseq, const int* __restrict__ seq_rows, const int* __restrict__ mask_pos,
+                      float invT, float* __restrict__ part, unsigned* __restrict__ row_count,
+                      unsigned* __restrict__ seq_count, int nseq, const int* __restrict__ seq_rows, const int* __restrict__ mask_pos,
                       const int* __restrict__ caps, float tau, float lambda,
                       float* __restrict__ row_H, float* H, int* argmax, float* maxprob,
                       int* selected, int* n_selected, float* running, const int* running_idx) {
@@ -365,25 +408,56 @@ entropy_select_kernel(const T* __restrict__ logits, int V, long ld, int splits, 
   reduce_range<T, kVec>(rp, c0, c1, a, st);
   st = block_reduce(st, a);
 
+  // Two-level finish, no waiting: the last CTA of a row merges the row's splits and
+  // writes its statistics; the last row of a sequence to finish applies the commit rule.
   __shared__ int s_last, s_seq;
   if (threadIdx.x == 0) {
-    // partial in scaled units: m_scaled = m_raw * invT (t already is in log2 units)
-    float4 v = make_float4(st.m * invT, st.s, st.u, __int_as_float(st.idx));
-    *reinterpret_cast<float4*>(part + ((long)row * splits + split) * 4) = v;
+    int last = 1;
+    if (splits > 1) {
+      // partial in scaled units: m_scaled = m_raw * invT (st is in log2 units)
+      float4 v = make_float4(st.m * invT, st.s, st.u, __int_as_float(st.idx));
+      *reinterpret_cast<float4*>(part + ((long)row * splits + split) * 4) = v;
+      __threadfence();
+      last = (atomicAdd(row_count + row, 1u) + 1 == (unsigned)splits);
+    }
+    s_last = last;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  if (splits > 1) {
+    __threadfence();
+    if (threadIdx.x < 32) {
+      Acc m;
+      acc_init(m);
+      for (int k = threadIdx.x; k < splits; k += 32)
+        acc_merge(m, load_partial(part + ((long)row * splits + k) * 4), kLog2e);
+      acc_warp_reduce(m, kLog2e);
+      if (threadIdx.x == 0) {
+        st = m;
+        row_count[row] = 0u;
+      }
+    }
+  } else if (threadIdx.x == 0) {
+    st.m *= invT;  // scaled units, as the merged partials
+  }
+  if (threadIdx.x == 0) {
+    const float h = kLn2 * (log2f(st.s) - st.u / st.s);
+    row_H[row] = h;
+    if (H) H[row] = h;
+    if (argmax) argmax[row] = st.idx;
+    if (maxprob) maxprob[row] = 1.f / st.s;
     __threadfence();
     const int b = find_seq(seq_rows, nseq, row);
-    const unsigned need = (unsigned)((seq_rows[b + 1] - seq_rows[b]) * splits);
-    const unsigned prev = atomicAdd(seq_count + b, 1u);
-    s_last = (prev + 1 == need);
+    const unsigned need = (unsigned)(seq_rows[b + 1] - seq_rows[b]);
+    s_last = (atomicAdd(seq_count + b, 1u) + 1 == need);
     s_seq = b;
   }
   __syncthreads();
   if (!s_last) return;
   __threadfence();
   const int b = s_seq;
-  finalize_sequence(b, seq_rows[b], seq_rows[b + 1], part, splits, 1, splits, tau, lambda,
-                    mask_pos, caps, row_H, H, argmax, maxprob, selected, n_selected, running,
-                    running_idx);
+  commit_rule(b, seq_rows[b], seq_rows[b + 1], tau, lambda, mask_pos, caps, row_H, selected,
+              n_selected, running, running_idx);
   if (threadIdx.x == 0) seq_count[b] = 0u;
 }
 
@@ -451,7 +525,8 @@ cudaError_t launch_select(const EntropyArgs& A, const EntropyScratch& W, int spl
   const dim3 grid((unsigned)(A.rows * splits));
   auto kern = vec ? entropy_select_kernel<T, true> : entropy_select_kernel<T, false>;
   return launch_pdl(kern, grid, dim3(kThreads), 0, st, (const T*)A.logits, A.V, A.ld, splits,
-                    split_cols, invT, W.partials, W.seq_count, A.nseq, A.seq_rows, A.mask_pos,
+                    split_cols, invT, W.partials, W.row_count, W.seq_count, A.nseq, A.seq_rows,
+                    A.mask_pos,
                     A.caps, A.tau, A.lambda, W.row_H, A.H, A.argmax, A.maxprob, A.selected,
                     A.n_selected, A.running, (const int*)A.running_idx);
 }
