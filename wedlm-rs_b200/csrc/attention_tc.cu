@@ -360,23 +360,51 @@ __global__ void attention_combine_kernel(const CombineItem* items, int nitems, A
   const int S = p.seq_rows[it.b];
   const int qi = it.t * kQT + qr;
   if (qi >= S * p.group) return;
+  // (m, l) of up to 32 parts at once: lane k holds part k; then the O rows of 8 parts
+  // per round, every load of a round in flight together
   float M = -INFINITY;
-  for (int k = 0; k < it.nparts; ++k) {
-    const float* ml = p.part_ml + ((long)(it.part0 + k) * kQT + qr) * 2;
-    if (ml[1] > 0.f) M = fmaxf(M, ml[0]);
+  for (int k0 = 0; k0 < it.nparts; k0 += 32) {
+    const int k = k0 + lane;
+    if (k < it.nparts) {
+      const float* ml = p.part_ml + ((long)(it.part0 + k) * kQT + qr) * 2;
+      if (ml[1] > 0.f) M = fmaxf(M, ml[0]);
+    }
   }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
   float acc[4] = {0.f, 0.f, 0.f, 0.f}, lsum = 0.f;
-  for (int k = 0; k < it.nparts; ++k) {
-    const long pi = (long)(it.part0 + k) * kQT + qr;
-    const float mk = p.part_ml[pi * 2], lk = p.part_ml[pi * 2 + 1];
-    if (!(lk > 0.f)) continue;
-    const float f = fast_exp2(mk - M);
-    lsum += f * lk;
-    const float4 v = *reinterpret_cast<const float4*>(p.part_o + pi * kD + lane * 4);
-    acc[0] += f * v.x;
-    acc[1] += f * v.y;
-    acc[2] += f * v.z;
-    acc[3] += f * v.w;
+  for (int k0 = 0; k0 < it.nparts; k0 += 32) {
+    const int nk = min(32, it.nparts - k0);
+    float f = 0.f, lk = 0.f;
+    if (lane < nk) {
+      const long pi = (long)(it.part0 + k0 + lane) * kQT + qr;
+      const float mk = p.part_ml[pi * 2];
+      lk = p.part_ml[pi * 2 + 1];
+      f = lk > 0.f ? fast_exp2(mk - M) : 0.f;
+    }
+    float fl = f * lk;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) fl += __shfl_xor_sync(0xffffffffu, fl, o);
+    lsum += fl;
+    for (int j0 = 0; j0 < nk; j0 += 8) {
+      float4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int kk = k0 + (j0 + j < nk ? j0 + j : j0);
+        v[j] = *reinterpret_cast<const float4*>(p.part_o + ((long)(it.part0 + kk) * kQT + qr) * kD +
+                                                lane * 4);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float fj = __shfl_sync(0xffffffffu, f, (j0 + j) & 31);
+        if (j0 + j < nk) {
+          acc[0] += fj * v[j].x;
+          acc[1] += fj * v[j].y;
+          acc[2] += fj * v[j].z;
+          acc[3] += fj * v[j].w;
+        }
+      }
+    }
   }
   const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
   const int r = p.seq_row0[it.b] + qi / p.group;
