@@ -112,6 +112,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
   uint64_t* o_done = p_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 1);
   int* s_rank = reinterpret_cast<int*>(tmem_slot + 4);  // window ranks of sequence b
+  int* s_krank = s_rank + 4096;                          // key ranks of the current chunk
 
   const AttnWork w = p.work[blockIdx.x];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -249,13 +250,24 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
           cm = fmaxf(cm, sv[j]);
         }
       } else {
+        // the chunk's key ranks, one key per softmax thread: cached keys rank below every
+        // query, keys past the window above; then key j is visible iff its rank <= mine
+        {
+          const int t = qr - (L - kbase);  // window index of key qr of this chunk
+          s_krank[qr] = t < 0 ? INT_MIN : (t < S ? s_rank[t] : INT_MAX);
+        }
+        named_bar_sync(1, 128);
+        const int4* kr4 = reinterpret_cast<const int4*>(s_krank);
 #pragma unroll
-        for (int j = 0; j < kKC; ++j) {
-          const int kp = kbase + j;
-          bool vis = kp < L;
-          if (!vis && kp < L + S) vis = s_rank[kp - L] <= my_rank;
-          sv[j] = vis ? sv[j] * p.scale_log2 : -INFINITY;
-          cm = fmaxf(cm, sv[j]);
+        for (int j4 = 0; j4 < kKC / 4; ++j4) {
+          const int4 rk = kr4[j4];
+          const int r4[4] = {rk.x, rk.y, rk.z, rk.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int j = j4 * 4 + e;
+            sv[j] = r4[e] <= my_rank ? sv[j] * p.scale_log2 : -INFINITY;
+            cm = fmaxf(cm, sv[j]);
+          }
         }
       }
       const float mn = fmaxf(m, cm);
@@ -523,7 +535,7 @@ Status run_attention_tc(const AttnArgs& a, const AttnPlan& plan, int* err, cudaS
   p.part_ml = plan.part_ml;
   p.scale_log2 = kLog2e / sqrtf((float)kD);
   p.err = err;
-  const size_t smem = 1024 + (2 + kStages * 4 + 2) * kBlk + 16 * 8 + 4096 * 4;
+  const size_t smem = 1024 + (2 + kStages * 4 + 2) * kBlk + 16 * 8 + 4096 * 4 + kKC * 4;
   int dev = 0;
   WEDLM_CUDA_TRY(cudaGetDevice(&dev));
   static unsigned attr_set = 0;
