@@ -611,7 +611,8 @@ def bench_block_attention(args, rank, ws, local):
             "gpu_launches": args.steps * 2,
             "roofline": {"bound": "tensor", "achieved": top["TFLOPs"], "peak": tflops_peak,
                          "peak_kind": peak_kind, "unit": "TFLOP/s", "frac": top["frac_tensor"],
-                         "traffic": None, "kernel": "attention_tc_kernel + attention_combine_kernel"}}
+                         "traffic": profile_traffic("attention_tc_block_8192.md"),
+                         "kernel": "attention_tc_kernel + attention_combine_kernel"}}
 
 
 # ----------------------------------------------------------------------------------
