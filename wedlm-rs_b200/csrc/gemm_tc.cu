@@ -659,11 +659,11 @@ GemmPlan plan_gemm_tc(int M, int N, int K, bool dual, int num_sms) {
   g.n_tiles = (N + kTileN - 1) / kTileN;
   // Weight tiles per unit: two tiles share each activation k-block, which halves the
   // shared memory the activations take per weight byte and so raises the weight bytes in
-  // flight per SM (LM head at 96 rows: 5.8 TB/s instead of 4.2).  Only for wide outputs:
-  // with few units per SM the larger units double the split-K partials of every CTA.
-  // Dual (gate/up) already shares the activations between two matrices, and above 128
-  // token rows the accumulators of two tiles would not double-buffer in TMEM.
-  int nb = (!dual && g.tok_tile <= 128 && (long)g.n_tiles * g.t_tiles >= 4L * num_sms) ? 2 : 1;
+  // flight per SM (LM head at 96 rows: 5.8 TB/s instead of 4.2; the layer GEMMs gain less,
+  // as the larger units double the split-K partials their consumers read).  Dual
+  // (gate/up) already shares the activations between two matrices, and above 128 token
+  // rows the accumulators of two tiles would not double-buffer in TMEM.
+  int nb = (!dual && g.tok_tile <= 128 && g.n_tiles >= 2) ? 2 : 1;
   if (const char* e = getenv("WEDLM_GEMM_NB")) nb = atoi(e) == 1 ? 1 : nb;
   g.nb = nb;
   const int na = dual ? 2 : 1;
