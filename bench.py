@@ -928,6 +928,49 @@ def cpu_baseline_decode(budget_s: float):
                                  "1 committed token per step (random-init entropy >> tau)"}
 
 
+def reference_attention(args, rank, ws):
+    """--impl reference for block_attention: the reference's attention (attention.rs:188-221:
+    scores, additive mask, softmax, weighted sum, GQA by repeating K/V) restated in numpy
+    f32 on the host cores, at the largest prefix (8192), same metric (TFLOP/s)."""
+    import os as _os
+    import numpy as np
+    L, S, nh, nkv, d = ATT_PREFIXES[-1], 96, 32, 8, 128
+    rng = np.random.default_rng(L)
+    q = rng.standard_normal((nh, S, d), dtype=np.float32)
+    k = rng.standard_normal((nkv, L + S, d), dtype=np.float32)
+    v = rng.standard_normal((nkv, L + S, d), dtype=np.float32)
+    rank_ = L + rng.permutation(S)
+    mask = np.zeros((S, L + S), np.float32)
+    mask[:, L:] = np.where(rank_[None, :] <= rank_[:, None], 0.0, -np.inf)
+
+    def step():
+        g = nh // nkv
+        kk, vv = np.repeat(k, g, axis=0), np.repeat(v, g, axis=0)
+        sc = q @ kk.transpose(0, 2, 1) / np.sqrt(d) + mask[None]
+        sc -= sc.max(axis=-1, keepdims=True)
+        p = np.exp(sc)
+        p /= p.sum(axis=-1, keepdims=True)
+        return p @ vv
+
+    for _ in range(max(1, args.warmup // 3)):
+        step()
+    n = max(2, min(args.steps, 5))
+    t0 = time.time()
+    for _ in range(n):
+        step()
+    s_per = (time.time() - t0) / n
+    val = attention_flops(L) / s_per / 1e12
+    return {"metric": METRIC, "value": round(val, 4), "unit": "TFLOP/s", "n_gpus": 1, "steps": n,
+            "warmup": args.warmup, "ms_per_step": round(s_per * 1e3, 2), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": "block_attention: 8B-shape GQA, 96-row window, prefix 8192, "
+                                   "causal over explicit positions"},
+            "cpu_baseline": {"value": round(val, 4), "unit": "TFLOP/s", "cores": _os.cpu_count(),
+                             "kind": "port", "sample": f"{n} full launches at prefix {L}, numpy f32 with BLAS threads"},
+            "e2e": {"value": round(val, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
 def reference_decode(args, rank, ws):
     """--impl reference for decode_8b: the reference's algorithm on the host cores (the
     oracle port; the Rust crate cannot be built without cargo and candle), each step a
@@ -991,7 +1034,14 @@ def main():
         ws = int(os.environ.get("WORLD_SIZE", "1"))
         if rank != 0:
             return
-        fn = reference_decode if args.workload == "decode_8b" else reference_entropy
+        fn = {"decode_8b": reference_decode, "serve_8b": reference_decode,
+              "entropy_select": reference_entropy,
+              "block_attention": reference_attention}.get(args.workload)
+        if fn is None:
+            print(json.dumps({"impl": "reference", "unavailable": "gemm_shapes times single "
+                              "kernels of this implementation; the reference has no such unit"}),
+                  flush=True)
+            return
         print(json.dumps(fn(args, rank, ws)), flush=True)
         return
 
