@@ -800,6 +800,19 @@ def bench_decode_8b(args, rank, ws, local):
     e2e_tok = est["tokens_generated"] * ws
     steps_timed = max(n1 - n0, 1)
 
+    # the reference benchmark's comparison: autoregressive decoding on the same model
+    # (engine.rs:160-217), one token per forward at the cached prompt
+    n_ar = 64
+    ctx.reset_sequence(0)
+    ctx.generate_autoregressive(prompt[:64], 4)
+    torch.cuda.synchronize()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ctx.reset_sequence(0)
+    a0.record(stream)
+    ar_ids = ctx.generate_autoregressive(prompt, n_ar)
+    a1.record(stream)
+    torch.cuda.synchronize()
+    ar_s = a0.elapsed_time(a1) / 1e3
     g = prof["gemm"]
     gemm_gbs = g["bytes"] / (g["ms"] * 1e-3) / 1e9 if g["ms"] > 0 else None
     a = prof["attention"]
@@ -839,6 +852,12 @@ def bench_decode_8b(args, rank, ws, local):
                                "launches_per_step": round(v["launches"] / max(args.profile_steps, 1), 1)}
                            for k, v in prof.items()},
         "profiled_step_ms": round(step_ms_prof, 3),
+        "ar_baseline": {"value": round(len(ar_ids) / ar_s, 2), "unit": "tok/s",
+                        "tokens": len(ar_ids),
+                        "scope": "wedlm_generate_autoregressive: 512-token prompt prefill + "
+                                 f"{n_ar} tokens, one per forward",
+                        "note": "random-init entropy >> tau, so WeDLM commits one token per "
+                                "96-row step here; with a trained model it commits several"},
     }
     ctx.close()
     del ctx

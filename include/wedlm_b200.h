@@ -267,6 +267,16 @@ WEDLM_API int wedlm_generate_with_stats(wedlm_ctx* ctx, int seq, const int32_t* 
                                         const wedlm_sampling_params* params, int32_t* out_ids,
                                         int32_t* n_out, wedlm_block_stats* stats, void* stream);
 
+/* WeDLMEngine::generate_autoregressive (src/engine.rs:160-217), the comparison baseline
+ * of the reference's benchmark: one token per forward, the argmax of the last position's
+ * logits (T = 0, last maximum on ties), until max_new_tokens or EOS.  The prompt is cached
+ * once and every step forwards only the newest token against the cache (the reference
+ * recomputes the whole sequence; the logits agree up to rounding).  out_ids (host)
+ * receives the generated ids, *n_out their count. */
+WEDLM_API int wedlm_generate_autoregressive(wedlm_ctx* ctx, int seq, const int32_t* prompt,
+                                            int n_prompt, int max_new_tokens, int32_t* out_ids,
+                                            int32_t* n_out, void* stream);
+
 /* Batched streaming decode: nseq independent sequences stepped together, one
  * forward per step over all live windows (data-parallel batching of
  * generate_streaming).  prompts: host [nseq, n_prompt]; out_ids: host

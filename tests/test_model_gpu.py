@@ -325,3 +325,21 @@ def test_c1_generate_with_stats_matches_oracle(c1):
     for k in ("steps", "tokens_generated", "block_size_reductions", "cache_refreshes"):
         assert st[k] == getattr(rst, k), k
     assert abs(st["avg_entropy"] - rst.avg_entropy) <= 1e-3
+
+
+def test_c1_autoregressive_matches_oracle(c1):
+    """generate_autoregressive (engine.rs:160-217): greedy one token per forward; the oracle
+    re-runs the whole sequence each token as the reference does."""
+    cfg, w, ctx, om = c1
+    prompt = np.random.default_rng(10).integers(1, 4095, size=20).tolist()
+    ids = ctx.generate_autoregressive(prompt, 12)
+    seq = list(prompt)
+    ref = []
+    for _ in range(12):
+        lg, _ = om.forward_with_positions(seq, list(range(len(seq))))
+        t = int(np.argmax(np.asarray(lg)[-1]))
+        ref.append(t)
+        seq.append(t)
+        if t == cfg.eos_token_id:
+            break
+    assert ids == ref

@@ -327,3 +327,88 @@ extern "C" int wedlm_generate_with_stats(wedlm_ctx* ctx, int seq, const int32_t*
   return WEDLM_OK;
 }
 
+
+// ---- autoregressive baseline -------------------------------------------------------------
+// WeDLMEngine::generate_autoregressive (src/engine.rs:160-217): one token per forward, the
+// argmax of the last position's logits (T = 0), until max_new tokens or EOS.  The
+// reference re-runs the whole sequence without a cache each token; here the prompt is
+// cached once and each step forwards only the newest token against the cache, which gives
+// the same logits up to rounding.  The argmax takes the last maximum (ties are not pinned
+// by the reference, whose argmax runs in candle).
+extern "C" int wedlm_generate_autoregressive(wedlm_ctx* ctx, int seq, const int32_t* prompt,
+                                             int n_prompt, int max_new_tokens, int32_t* out_ids,
+                                             int32_t* n_out, void* stream) {
+  using namespace wedlm;
+  if (int rc = block_guard(ctx)) return rc;
+  ModelState* m = ctx->model;
+  if (seq < 0 || seq >= m->max_seqs || !prompt || n_prompt < 1 || max_new_tokens < 0 || !out_ids ||
+      !n_out || n_prompt + max_new_tokens > m->max_ctx)
+    return ctx->fail(Status::err(WEDLM_ERR_INVALID_ARG, "bad sequence / prompt / lengths (max_ctx)"));
+  cudaStream_t st = (cudaStream_t)stream;
+  const int eos = m->cfg.eos_token_id;
+  BlockBuffers B;
+  Status s = B.alloc(m, 1);
+  if (s.good() && n_prompt > 1) s = prefill_ids(ctx, seq, prompt, n_prompt - 1, st);
+  if (s.good() && n_prompt == 1) {
+    m->cache_len[seq] = 0;
+    m->pending_rows[seq] = 0;
+  }
+  int last = prompt[n_prompt - 1];
+  int n = 0;
+  while (s.good() && n < max_new_tokens) {
+    std::vector<SeqSlice> sl(1);
+    sl[0].slot = seq;
+    sl[0].rows = 1;
+    sl[0].logit_begin = 0;
+    const int pos = m->cache_len[seq];
+    int nl = 0;
+    s = model_forward(ctx, sl, &last, &pos, nullptr, B.logits, m->dt, &nl, st);
+    if (!s.good()) break;
+    m->cache_len[seq] += 1;  // the token's K/V enter the cache
+    m->pending_rows[seq] = 0;
+    // argmax of the one row through the fused pass (its selection part is unused)
+    int* hi = B.h_io;
+    hi[0] = 0;
+    hi[1] = 1;
+    hi[2] = 0;
+    hi[3] = 1;
+    s = Status::ok();
+    cudaError_t e = cudaMemcpyAsync(B.d_io, hi, 4 * sizeof(int), cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) {
+      s = Status::err(WEDLM_ERR_CUDA, cudaGetErrorString(e));
+      break;
+    }
+    int* dout = B.d_io + 3 + B.cap;
+    EntropyArgs A;
+    A.logits = B.logits;
+    A.dtype = m->dt;
+    A.rows = 1;
+    A.V = m->vshard;
+    A.ld = m->vshard;
+    A.nseq = 1;
+    A.seq_rows = B.d_io;
+    A.mask_pos = B.d_io + 2;
+    A.caps = B.d_io + 3;
+    A.argmax = dout + B.cap;
+    A.selected = dout + 2 * B.cap;
+    A.n_selected = dout + 3 * B.cap;
+    EntropyPlan ep = plan_entropy(1, m->vshard, m->dt, ctx->num_sms);
+    s = ensure_entropy_scratch(ctx, 1, 1, (long)ep.splits * 4);
+    if (s.good()) s = run_entropy_select(A, ctx->ent, ctx->num_sms, st);
+    if (!s.good()) break;
+    int next = 0;
+    e = cudaMemcpyAsync(&next, A.argmax, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) {
+      s = Status::err(WEDLM_ERR_CUDA, cudaGetErrorString(e));
+      break;
+    }
+    out_ids[n++] = next;
+    last = next;
+    if (next == eos) break;
+  }
+  if (s.good()) s = check_device_error(ctx, st);
+  if (!s.good()) return ctx->fail(s);
+  *n_out = n;
+  return WEDLM_OK;
+}

@@ -97,6 +97,7 @@ _PROTOS = {
                                        C.POINTER(WedlmSamplingParams), P,
                                        C.POINTER(WedlmBlockStats), P]),
     "wedlm_commit_block": (C.c_int, [P, C.c_int, P, C.c_int, P]),
+    "wedlm_generate_autoregressive": (C.c_int, [P, C.c_int, P, C.c_int, C.c_int, P, I32P, P]),
     "wedlm_generate_with_stats": (C.c_int, [P, C.c_int, P, C.c_int, C.c_int, C.c_int,
                                             C.POINTER(WedlmSamplingParams), P, I32P,
                                             C.POINTER(WedlmBlockStats), P]),

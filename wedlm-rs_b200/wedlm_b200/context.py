@@ -368,6 +368,17 @@ class Context:
         stats = {f: getattr(st, f) for f, _ in WedlmBlockStats._fields_}
         return list(p) + out.tolist(), out.tolist(), stats
 
+    def generate_autoregressive(self, prompt, max_new_tokens: int, seq: int = 0, stream=None):
+        """``WeDLMEngine::generate_autoregressive`` at T = 0: returns the generated ids."""
+        import numpy as np
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(max(max_new_tokens, 1), np.int32)
+        n = C.c_int32()
+        check(lib().wedlm_generate_autoregressive(self.h, seq, p.ctypes.data, p.size,
+                                                  max_new_tokens, out.ctypes.data, C.byref(n),
+                                                  stream_ptr(stream)), self.h)
+        return out[:n.value].tolist()
+
     def commit_block(self, block, seq: int = 0, stream=None) -> None:
         """``WeDLMDecoder::commit_block_to_cache``."""
         import numpy as np
