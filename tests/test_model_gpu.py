@@ -343,3 +343,56 @@ def test_c1_autoregressive_matches_oracle(c1):
         if t == cfg.eos_token_id:
             break
     assert ids == ref
+
+
+def test_vocab_sharded_lm_head_and_entropy():
+    """The vocabulary-sharded path on one GPU: two contexts holding the LM-head rows
+    [0, V/2) and [V/2, V) give the full model's logits side by side, and their per-row
+    entropy partials (wedlm_entropy_partials) combined (wedlm_entropy_combine) give the
+    full-vocabulary entropy, argmax and selection, as the NCCL all-gather between GPUs
+    would."""
+    from wedlm_b200 import Context
+    cfg = long_ctx_bf16_config()
+    w = random_weights(cfg, seed=5, std=0.02)
+    V, half = cfg.vocab_size, cfg.vocab_size // 2
+    rng = np.random.default_rng(12)
+    prompt = rng.integers(0, V - 2, size=40)
+    win = rng.integers(0, V - 2, size=24)
+    win[[3, 7, 8, 15, 20]] = cfg.mask_token_id
+    pos = np.arange(40, 64)
+    out = []
+    for lo, hi in [(0, 0), (0, half), (half, V)]:
+        mc = to_model_config(cfg, max_block_tokens=32)
+        mc.vocab_shard_begin, mc.vocab_shard_end = lo, hi
+        ctx = Context(mc, max_seqs=1, max_ctx=128)
+        try:
+            ctx.load_weights(w)
+            ctx.reset_sequence(0)
+            ctx.prefill(0, prompt)
+            out.append(ctx.forward_with_positions([0], win[None], pos[None],
+                                                  logits_dtype=torch.float32).clone())
+            ctx.check_device_error()
+        finally:
+            ctx.close()
+    full, a, b = out
+    joined = torch.cat([a, b], dim=1)
+    assert full.shape == joined.shape
+    assert (full - joined).abs().max().item() <= 1e-4 * full.abs().max().item()
+    kc = Context(None)
+    try:
+        rows = full.shape[0]
+        sr = torch.tensor([0, rows], dtype=torch.int32, device="cuda")
+        mp = torch.arange(rows, dtype=torch.int32, device="cuda")
+        cp = torch.tensor([4], dtype=torch.int32, device="cuda")
+        ref = kc.entropy_select(full.contiguous(), 0.0, 8.5, 0.01, sr, mp, cp)
+        parts = torch.stack([kc.entropy_partials(a.contiguous(), 0, 0.0),
+                             kc.entropy_partials(b.contiguous(), half, 0.0)])
+        got = kc.entropy_combine(parts, 8.5, 0.01, sr, mp, cp)
+        torch.cuda.synchronize()
+    finally:
+        kc.close()
+    assert torch.equal(got["argmax"], ref["argmax"])
+    assert (got["H"] - ref["H"]).abs().max().item() <= 1e-4
+    n = int(ref["n_selected"][0])
+    assert int(got["n_selected"][0]) == n
+    assert torch.equal(got["selected"][:n], ref["selected"][:n])
