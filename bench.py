@@ -730,9 +730,21 @@ def bench_decode_8b(args, rank, ws, local):
     if args.layers != 36 and not args.profile:
         raise SystemExit("--layers only applies to --profile runs (captures of a reduced model)")
     cfg = ModelConfig.wedlm_8b(max_block_tokens=WINDOW_8B, num_hidden_layers=args.layers)
+    # vocabulary-sharded LM head + entropy pass over the ranks (NCCL all-gathers of the
+    # final-normed rows and of the per-row partials), or plain data parallelism
+    sharded = ws > 1 and args.lm_head == "vocab"
+    if sharded:
+        V = cfg.vocab_size
+        cfg.vocab_shard_begin, cfg.vocab_shard_end = rank * V // ws, (rank + 1) * V // ws
     max_ctx = PROMPT_8B + NEW_8B + WINDOW_8B + 64
     ctx = Context(cfg, device=local, max_seqs=1, max_ctx=max_ctx)
     ctx.init_random(seed=0, std=0.02)
+    if sharded:
+        import torch.distributed as dist
+        from wedlm_b200 import comm_unique_id
+        uid = [comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        ctx.comm_init(uid[0], rank, ws, timeout_ms=120000)
     prompt = make_prompt(PROMPT_8B, seed=rank)
     params = balanced_params()
     stream = torch.cuda.current_stream()
@@ -797,22 +809,36 @@ def bench_decode_8b(args, rank, ws, local):
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_s = max_over_ranks(e0.elapsed_time(e1) / 1e3, ws)
-    e2e_tok = est["tokens_generated"] * ws
+    e2e_tok = float(est["tokens_generated"])
+    e2e_steps = float(est["steps"])
+    if ws > 1:
+        import torch.distributed as dist
+        t = torch.tensor([e2e_tok, e2e_steps], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t)
+        e2e_tok, e2e_steps = float(t[0].item()), float(t[1].item()) / ws
     steps_timed = max(n1 - n0, 1)
 
     # the reference benchmark's comparison: autoregressive decoding on the same model
-    # (engine.rs:160-217), one token per forward at the cached prompt
+    # (engine.rs:160-217), one token per forward at the cached prompt (it needs the whole
+    # vocabulary on the context, so the vocabulary-sharded run leaves it out)
     n_ar = 64
-    ctx.reset_sequence(0)
-    ctx.generate_autoregressive(prompt[:64], 4)
-    torch.cuda.synchronize()
-    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ctx.reset_sequence(0)
-    a0.record(stream)
-    ar_ids = ctx.generate_autoregressive(prompt, n_ar)
-    a1.record(stream)
-    torch.cuda.synchronize()
-    ar_s = a0.elapsed_time(a1) / 1e3
+    ar = None
+    if not sharded:
+        ctx.reset_sequence(0)
+        ctx.generate_autoregressive(prompt[:64], 4)
+        torch.cuda.synchronize()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ctx.reset_sequence(0)
+        a0.record(stream)
+        ar_ids = ctx.generate_autoregressive(prompt, n_ar)
+        a1.record(stream)
+        torch.cuda.synchronize()
+        ar_s = a0.elapsed_time(a1) / 1e3
+        ar = {"value": round(len(ar_ids) / ar_s, 2), "unit": "tok/s", "tokens": len(ar_ids),
+              "scope": "wedlm_generate_autoregressive: 512-token prompt prefill + "
+                       f"{n_ar} tokens, one per forward",
+              "note": "random-init entropy >> tau, so WeDLM commits one token per "
+                      "96-row step here; with a trained model it commits several"}
     g = prof["gemm"]
     gemm_gbs = g["bytes"] / (g["ms"] * 1e-3) / 1e9 if g["ms"] > 0 else None
     a = prof["attention"]
@@ -830,13 +856,16 @@ def bench_decode_8b(args, rank, ws, local):
                    "ffn": 12288, "vocab": 151936, "window": WINDOW_8B,
                    "tokens_per_step": round(toks / args.steps, 3),
                    "l2": "inputs larger than L2 (15.1 GB of weights streamed per step)",
-                   "parallelism": f"dp{ws} (one independent sequence per GPU)"},
+                   "parallelism": (f"dp{ws} sequences + LM head and entropy pass vocabulary-"
+                                   f"sharded over {ws} GPUs (NCCL all-gathers)" if sharded else
+                                   f"dp{ws} (one independent sequence per GPU)")},
         "clocks": clocks,
         "e2e": {"value": round(e2e_tok / e2e_s, 2), "unit": "committed tok/s",
                 "h2d_bytes_per_step": int((h1 - h0) / steps_timed),
                 "d2h_bytes_per_step": int((d1 - d0) / steps_timed),
-                "scope": "wedlm_generate_streaming: 512-token prompt prefill + 512 tokens, "
-                         "host ids in and out"},
+                "tokens": int(e2e_tok), "steps_per_sequence": round(e2e_steps, 1),
+                "scope": "wedlm_generate_streaming: 512-token prompt prefill + up to 512 "
+                         "tokens (fewer when EOS is generated), host ids in and out"},
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm", "achieved": round(gemm_gbs, 1) if gemm_gbs else None,
                      "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s",
@@ -852,12 +881,7 @@ def bench_decode_8b(args, rank, ws, local):
                                "launches_per_step": round(v["launches"] / max(args.profile_steps, 1), 1)}
                            for k, v in prof.items()},
         "profiled_step_ms": round(step_ms_prof, 3),
-        "ar_baseline": {"value": round(len(ar_ids) / ar_s, 2), "unit": "tok/s",
-                        "tokens": len(ar_ids),
-                        "scope": "wedlm_generate_autoregressive: 512-token prompt prefill + "
-                                 f"{n_ar} tokens, one per forward",
-                        "note": "random-init entropy >> tau, so WeDLM commits one token per "
-                                "96-row step here; with a trained model it commits several"},
+        "ar_baseline": ar,
     }
     ctx.close()
     del ctx
@@ -1037,6 +1061,9 @@ def main():
     ap.add_argument("--shard", default="vocab", choices=["vocab", "dp"],
                     help="entropy_select on N > 1 GPUs: shard the vocabulary (NCCL combine of "
                          "per-row partials) or run independent batches")
+    ap.add_argument("--lm-head", default="dp", choices=["vocab", "dp"],
+                    help="decode_8b on N > 1 GPUs: vocabulary-shard the LM head and the "
+                         "entropy pass over the ranks, or keep a whole LM head per GPU")
     ap.add_argument("--hold-seconds", type=float, default=1.0)
     ap.add_argument("--layers", type=int, default=36,
                     help="decoder layers of the decode_8b model (only with --profile: small "

@@ -214,6 +214,31 @@ WEDLM_API int wedlm_entropy_combine(wedlm_ctx* ctx, const float* partials, int n
                           int32_t* argmax, float* maxprob, int32_t* selected,
                           int32_t* n_selected, void* stream);
 
+/* ---- multi-GPU: vocabulary-sharded LM head and entropy pass ------------------------- */
+
+/* The reference runs on one device and has no collective; these replace nothing in it.
+ * One process per GPU, one context per process.  wedlm_comm_unique_id writes the 128-byte
+ * NCCL unique id (ncclGetUniqueId) to `out`; make it on one rank and pass it to every
+ * rank.  wedlm_comm_init (collective over nranks) joins the context to an NCCL
+ * communicator; the ranks' configs must hold vocab shards that tile [0, V) in rank order
+ * (rank r: [vocab_shard_begin, vocab_shard_end)), otherwise WEDLM_ERR_INVALID_ARG.
+ * Every wait on the communicator (init, each decode step) gives up after timeout_ms,
+ * aborts the communicator and returns WEDLM_ERR_TIMEOUT.  NCCL is loaded at run time
+ * (libnccl.so.2; WEDLM_ERR_UNSUPPORTED when it is absent).
+ * With a communicator, the decode loops below (wedlm_decode_begin / step, streaming and
+ * streaming-batch generation) run the LM head and the entropy pass vocabulary-sharded:
+ * each rank decodes its own sequences, the final-normed mask rows and the per-row
+ * softmax partials are all-gathered, and each rank applies the commit rule to its rows.
+ * They are then collective: every rank calls wedlm_decode_begin, and every rank calls
+ * wedlm_decode_step with the same n_steps until it reports n_live == 0 (n_live counts
+ * the sequences of all ranks that were live at the step's start).  Block mode and the
+ * autoregressive loop need the whole vocabulary on the context.
+ * wedlm_comm_destroy (collective) releases the communicator; wedlm_destroy also does. */
+WEDLM_API int wedlm_comm_unique_id(void* out, int nbytes);
+WEDLM_API int wedlm_comm_init(wedlm_ctx* ctx, const void* unique_id, int rank, int nranks,
+                              int timeout_ms);
+WEDLM_API int wedlm_comm_destroy(wedlm_ctx* ctx);
+
 /* ---- decode loops --------------------------------------------------------------- */
 
 /* WeDLMDecoder::generate_streaming (src/decoding/wedlm.rs:336-590) on sequence

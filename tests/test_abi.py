@@ -50,3 +50,10 @@ def test_config_struct_layout():
     assert c.vocab_size == 151936 and c.num_key_value_heads == 8 and c.dtype == 1
     # layout: 8 int32, 2 double, 7 int32 (with padding after the first 8 ints: none)
     assert ctypes.sizeof(WedlmConfig) == 8 * 4 + 2 * 8 + 7 * 4 + 4
+
+
+def test_comm_unique_id_without_gpu():
+    """The NCCL unique id needs no device (NCCL is loaded at run time by the library)."""
+    from wedlm_b200 import comm_unique_id
+    a, b = comm_unique_id(), comm_unique_id()
+    assert len(a) == 128 and len(b) == 128 and a != b

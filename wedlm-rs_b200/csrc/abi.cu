@@ -4,6 +4,7 @@
 #include <cstring>
 #include <new>
 
+#include "comm.h"
 #include "context.h"
 #include "model.h"
 #include "gemm.h"
@@ -199,6 +200,7 @@ void wedlm_destroy(wedlm_ctx* ctx) {
   cudaSetDevice(ctx->device);
   cudaDeviceSynchronize();
   wedlm::session_free(ctx);
+  wedlm::comm_free(ctx);
   wedlm::free_attention_kernel_scratch(ctx);
   for (cudaEvent_t e : ctx->prof.ev) cudaEventDestroy(e);
   wedlm::model_destroy(ctx);

@@ -260,12 +260,17 @@ Status check_block_args(wedlm_ctx* ctx, int seq, int block_size, const wedlm_sam
   return Status::ok();
 }
 
-int block_guard(wedlm_ctx* ctx) {
+// needs_vocab: the call projects and selects over the whole vocabulary on this context.
+int block_guard(wedlm_ctx* ctx, bool needs_vocab = true) {
   if (!ctx) return WEDLM_ERR_INVALID_ARG;
   if (!ctx->model) return ctx->fail(Status::err(WEDLM_ERR_STATE, "context has no model"));
   cudaError_t e = cudaSetDevice(ctx->device);
   if (e != cudaSuccess) return ctx->fail(Status::err(WEDLM_ERR_CUDA, cudaGetErrorString(e)));
   if (ctx->session) return ctx->fail(Status::err(WEDLM_ERR_STATE, "a decode session is active"));
+  if (needs_vocab && ctx->model->vshard != ctx->model->V)
+    return ctx->fail(Status::err(WEDLM_ERR_STATE,
+                                 "this context holds a vocabulary shard; block mode and the "
+                                 "autoregressive loop need the whole vocabulary"));
   return WEDLM_OK;
 }
 
@@ -298,7 +303,7 @@ extern "C" int wedlm_generate_block(wedlm_ctx* ctx, int seq, const int32_t* pref
 
 extern "C" int wedlm_commit_block(wedlm_ctx* ctx, int seq, const int32_t* block, int n,
                                   void* stream) {
-  if (int rc = wedlm::block_guard(ctx)) return rc;
+  if (int rc = wedlm::block_guard(ctx, false)) return rc;
   if (seq < 0 || seq >= ctx->model->max_seqs || !block || n < 1 ||
       ctx->model->cache_len[seq] + n > ctx->model->max_ctx)
     return ctx->fail(Status::err(WEDLM_ERR_INVALID_ARG, "bad sequence / block"));

@@ -13,6 +13,7 @@ namespace wedlm {
 struct ModelState;
 struct DecodeSession;
 struct AttnKernelScratch;
+struct Comm;
 }
 
 // Optional per-kernel-class timing with CUDA events on the launching stream
@@ -59,6 +60,8 @@ struct wedlm_ctx {
   wedlm::DecodeSession* session = nullptr;
   // stand-alone block attention (attention_kernel.cu)
   wedlm::AttnKernelScratch* att = nullptr;
+  // NCCL communicator of the vocabulary-sharded decode (comm.cu); NULL on one GPU
+  wedlm::Comm* comm = nullptr;
 
   int fail(const wedlm::Status& s) {
     last_error = s.msg;

@@ -12,10 +12,19 @@
 // argmax on the device (:511-548); the selected slots are filled (:553-572).
 // Host <-> device per step: the forward's metadata upload, one upload of the
 // selection inputs, one download of the results.
+//
+// With a communicator (comm.cu) the LM head and the entropy pass are vocabulary-sharded:
+// every rank runs the backbone over its own sequences' windows, the final-normed mask
+// rows of all ranks are all-gathered, each rank projects every rank's rows onto its own
+// LM-head rows and reduces them to per-row partials (max, sum of exponentials, entropy
+// sum, argmax), the partials are all-gathered, and each rank combines the shards for its
+// own rows and applies the commit rule.  Both gathers run on NCCL over NVLink; the ranks
+// step in lock step until no rank has a live sequence.
 #include <algorithm>
 #include <cstring>
 #include <vector>
 
+#include "comm.h"
 #include "entropy_select.cuh"
 #include "model.h"
 
@@ -57,8 +66,23 @@ struct DecodeSession {
   std::vector<SeqSlice> slices;
   int64_t h2d_bytes = 0, d2h_bytes = 0, steps = 0;
 
+  // Vocabulary-sharded step: rows per rank in the gathered buffers (the largest window
+  // capacity of any rank), the header gather (per rank: live sequences, mask rows) and
+  // the buffers of the hidden-row and partials gathers.
+  bool sharded = false;
+  int rmax = 0;
+  int* shdr = nullptr;  // device: send [4] | recv [4 * nranks]
+  uint8_t* sblock = nullptr;
+  void* hsend = nullptr;    // [rmax, H] model dtype
+  void* hrecv = nullptr;    // [nranks * rmax, H]
+  void* slogits = nullptr;  // [nranks * rmax, vshard]
+  float* psend = nullptr;   // [nranks * rmax, 4]
+  float* precv = nullptr;   // [nranks, nranks * rmax, 4]
+
   ~DecodeSession() {
     cudaFree(block);
+    cudaFree(shdr);
+    cudaFree(sblock);
     if (h_in) cudaFreeHost(h_in);
     if (h_out) cudaFreeHost(h_out);
   }
@@ -70,6 +94,44 @@ void session_free(wedlm_ctx* ctx) {
 }
 
 namespace {
+
+// Sharded session set-up (collective: every rank of the communicator calls it): agree on
+// the rows per rank of the gathered buffers and allocate them.
+Status sharded_begin(wedlm_ctx* ctx, DecodeSession* S, cudaStream_t st) {
+  ModelState* m = ctx->model;
+  Comm* c = ctx->comm;
+  const int n = comm_size(c);
+  WEDLM_CUDA_TRY(cudaMalloc(&S->shdr, sizeof(int) * 4 * (n + 1)));
+  WEDLM_CUDA_TRY(cudaMemsetAsync(S->shdr, 0, sizeof(int) * 4 * (n + 1), st));
+  S->h_in[0] = S->rows_cap;
+  WEDLM_CUDA_TRY(cudaMemcpyAsync(S->shdr, S->h_in, sizeof(int), cudaMemcpyHostToDevice, st));
+  GatherPiece g;
+  g.send = S->shdr;
+  g.recv = S->shdr + 4;
+  g.count = 1;
+  g.dtype = kCommInt32;
+  WEDLM_TRY(comm_all_gather(c, &g, 1, st));
+  WEDLM_CUDA_TRY(cudaMemcpyAsync(S->h_out, S->shdr + 4, sizeof(int) * n, cudaMemcpyDeviceToHost, st));
+  WEDLM_TRY(comm_sync(c, st));
+  int rmax = 0;
+  for (int r = 0; r < n; ++r) rmax = std::max(rmax, S->h_out[r]);
+  S->rmax = rmax;
+  const size_t H = m->H, es = m->esz, rows = (size_t)n * rmax;
+  auto up = [](size_t b) { return (b + 255) / 256 * 256; };
+  const size_t b_hs = up((size_t)rmax * H * es), b_hr = up(rows * H * es),
+               b_lg = up(rows * m->vshard * es), b_ps = up(rows * 4 * 4),
+               b_pr = up((size_t)n * rows * 4 * 4);
+  WEDLM_CUDA_TRY(cudaMalloc(&S->sblock, b_hs + b_hr + b_lg + b_ps + b_pr));
+  S->hsend = S->sblock;
+  S->hrecv = S->sblock + b_hs;
+  S->slogits = S->sblock + b_hs + b_hr;
+  S->psend = reinterpret_cast<float*>(S->sblock + b_hs + b_hr + b_lg);
+  S->precv = reinterpret_cast<float*>(S->sblock + b_hs + b_hr + b_lg + b_ps);
+  // rows past a rank's mask rows are projected too: keep them finite
+  WEDLM_CUDA_TRY(cudaMemsetAsync(S->hsend, 0, b_hs + b_hr, st));
+  S->sharded = true;
+  return Status::ok();
+}
 
 Status session_begin(wedlm_ctx* ctx, const std::vector<int>& slots, const int32_t* prompts,
                      int n_prompt, int max_new, int window, const wedlm_sampling_params& prm,
@@ -87,6 +149,10 @@ Status session_begin(wedlm_ctx* ctx, const std::vector<int>& slots, const int32_
                   "only temperature 0 (greedy) is supported: the reference samples with an "
                   "unseeded RNG at T > 0");
   WEDLM_CHECK_ARG(n_prompt + max_new + window <= m->max_ctx, "prompt + generation exceed max_ctx");
+  if (!ctx->comm && m->vshard != m->V)
+    return Status::err(WEDLM_ERR_STATE,
+                       "this context holds a vocabulary shard: decoding needs the whole "
+                       "vocabulary or a communicator (wedlm_comm_init)");
   session_free(ctx);
   DecodeSession* S = new DecodeSession();
   ctx->session = S;
@@ -129,18 +195,94 @@ Status session_begin(wedlm_ctx* ctx, const std::vector<int>& slots, const int32_
   S->rows_cap = B * window;
   S->nseq_cap = B;
   const size_t lbytes = ((size_t)S->rows_cap * m->vshard * m->esz + 255) / 256 * 256;
-  const size_t in_ints = (size_t)3 * B + 1 + S->rows_cap;
+  const size_t in_ints = (size_t)3 * B + 1 + S->rows_cap + 4;  // + the sharded step's header
   const size_t out_ints = (size_t)3 * S->rows_cap + B;
+  const int nranks = ctx->comm ? comm_size(ctx->comm) : 1;
   WEDLM_CUDA_TRY(cudaMalloc(&S->block, lbytes + (in_ints + B + out_ints) * 4 + 1024));
   S->logits = S->block;
   S->d_in = reinterpret_cast<int*>(S->block + lbytes);
   S->running = reinterpret_cast<float*>(S->d_in + in_ints);
   S->d_out = reinterpret_cast<int*>(S->running + B);
   WEDLM_CUDA_TRY(cudaMallocHost(&S->h_in, in_ints * 4 + 64));
-  WEDLM_CUDA_TRY(cudaMallocHost(&S->h_out, out_ints * 4 + 64));
+  WEDLM_CUDA_TRY(cudaMallocHost(&S->h_out, (out_ints + 1 + 4 * nranks) * 4 + 64));
   std::vector<float> r0(B, prm.entropy_threshold);  // running entropy starts at tau (:370)
   WEDLM_CUDA_TRY(cudaMemcpyAsync(S->running, r0.data(), B * 4, cudaMemcpyHostToDevice, st));
+  if (ctx->comm) WEDLM_TRY(sharded_begin(ctx, S, st));
   WEDLM_CUDA_TRY(cudaStreamSynchronize(st));
+  return Status::ok();
+}
+
+// Vocabulary-sharded selection of one step (collective).  On entry the forward has
+// written this rank's final-normed mask rows to S->hsend and the host staging holds the
+// selection inputs (nin ints).  Gathers the hidden rows and headers, projects every
+// rank's rows onto this rank's LM-head rows, reduces them to per-row partials, gathers
+// the partials, combines this rank's rows and applies the commit rule; downloads the
+// results, the device error word and the headers, and waits (bounded).  *global_live =
+// live sequences of all ranks at the start of the step.
+Status sharded_select(wedlm_ctx* ctx, DecodeSession* S, EntropyArgs& A, int nin,
+                      long* global_live) {
+  ModelState* m = ctx->model;
+  Comm* c = ctx->comm;
+  cudaStream_t st = S->st;
+  const int n = comm_size(c), me = comm_rank(c);
+  const int rows = n * S->rmax;
+  // scratch first: growing it synchronises the device
+  const EntropyPlan ep = plan_entropy(rows, m->vshard, m->dt, ctx->num_sms);
+  WEDLM_TRY(ensure_entropy_scratch(ctx, rows, std::max(A.nseq, 1), (long)rows * ep.splits * 4));
+  int* hdr = S->h_in + nin;
+  hdr[0] = A.nseq;
+  hdr[1] = A.rows;
+  hdr[2] = hdr[3] = 0;
+  WEDLM_CUDA_TRY(cudaMemcpyAsync(S->d_in, S->h_in, (size_t)(nin + 4) * 4, cudaMemcpyHostToDevice, st));
+  S->h2d_bytes += (nin + 4) * 4;
+
+  GatherPiece g[2];
+  g[0].send = S->hsend;
+  g[0].recv = S->hrecv;
+  g[0].count = (size_t)S->rmax * m->H;
+  g[0].dtype = m->dt;
+  g[1].send = S->d_in + nin;
+  g[1].recv = S->shdr + 4;
+  g[1].count = 4;
+  g[1].dtype = kCommInt32;
+  WEDLM_TRY(comm_all_gather(c, g, 2, st));
+
+  WEDLM_TRY(model_lm_head(ctx, S->hrecv, m->H, rows, S->slogits, m->dt, st));
+
+  EntropyArgs P;
+  P.logits = S->slogits;
+  P.dtype = m->dt;
+  P.rows = rows;
+  P.V = m->vshard;
+  P.ld = m->vshard;
+  P.temperature = A.temperature;
+  int ph = prof_begin(ctx, st);
+  WEDLM_TRY(run_entropy_partials(P, ctx->ent, comm_shard_begin(c, me), S->psend, ctx->num_sms, st));
+  prof_end(ctx, st, ph, WedlmProfiler::kEntropy, (double)rows * m->vshard * m->esz, 0, 1);
+
+  GatherPiece gp;
+  gp.send = S->psend;
+  gp.recv = S->precv;
+  gp.count = (size_t)rows * 4;
+  gp.dtype = WEDLM_F32;
+  WEDLM_TRY(comm_all_gather(c, &gp, 1, st));
+
+  if (A.rows > 0) {
+    ph = prof_begin(ctx, st);
+    WEDLM_TRY(run_entropy_combine(S->precv + (size_t)me * S->rmax * 4, n, A, ctx->ent, st, rows));
+    prof_end(ctx, st, ph, WedlmProfiler::kEntropy, (double)n * A.rows * 16, 0, 1);
+  }
+  const size_t nout = (size_t)3 * S->rows_cap + A.nseq;
+  int* ho = S->h_out;
+  WEDLM_CUDA_TRY(cudaMemcpyAsync(ho, S->d_out, nout * 4, cudaMemcpyDeviceToHost, st));
+  WEDLM_CUDA_TRY(cudaMemcpyAsync(ho + nout, ctx->dev_err, 4, cudaMemcpyDeviceToHost, st));
+  WEDLM_CUDA_TRY(cudaMemcpyAsync(ho + nout + 1, S->shdr + 4, sizeof(int) * 4 * n,
+                                 cudaMemcpyDeviceToHost, st));
+  S->d2h_bytes += (int64_t)(nout + 1 + 4 * n) * 4;
+  WEDLM_TRY(comm_sync(c, st));
+  long live = 0;
+  for (int r = 0; r < n; ++r) live += ho[nout + 1 + 4 * r];
+  *global_live = live;
   return Status::ok();
 }
 
@@ -187,18 +329,21 @@ Status session_step(wedlm_ctx* ctx, int* live_after) {
     S->slices.push_back(sl);
     S->live.push_back(b);
   }
-  if (S->live.empty()) {
+  if (S->live.empty() && !S->sharded) {
     *live_after = 0;
     return Status::ok();
   }
-  S->steps += 1;
+  if (!S->live.empty()) S->steps += 1;
   const int R_rows = (int)S->tok.size();
   S->h2d_bytes += (int64_t)(7 * R_rows + 4 * (int)S->live.size()) * 4;
 
   // ---- step C: one forward over every live window ----
+  // (sharded: the LM head runs after the gather; the forward stops at the final norm)
   int nl = 0;
-  WEDLM_TRY(model_forward(ctx, S->slices, S->tok.data(), S->pos.data(), nullptr, S->logits, m->dt,
-                          &nl, st));
+  if (!S->live.empty())
+    WEDLM_TRY(model_forward(ctx, S->slices, S->tok.data(), S->pos.data(), nullptr,
+                            S->sharded ? nullptr : S->logits, m->dt, &nl, st,
+                            S->sharded ? S->hsend : nullptr));
 
   // ---- steps D, D': commit, drain, refill ----
   for (int b : S->live) {
@@ -252,53 +397,62 @@ Status session_step(wedlm_ctx* ctx, int* live_after) {
     h_caps[k] = S->prm.max_tokens_per_step;
     h_ridx[k] = S->live[k];
   }
-  if (rr > 0) {
-    const int nin = nb + 1 + rr + 2 * nb;
+  const int nin = nb + 1 + rr + 2 * nb;
+  int* d_rows = S->d_in;
+  int* d_mpos = d_rows + nb + 1;
+  int* d_caps = d_mpos + rr;
+  int* d_ridx = d_caps + nb;
+  float* dH = reinterpret_cast<float*>(S->d_out);
+  int* dA = S->d_out + S->rows_cap;
+  int* dS = dA + S->rows_cap;
+  int* dN = dS + S->rows_cap;
+  EntropyArgs A;
+  A.dtype = m->dt;
+  A.rows = rr;
+  A.temperature = S->prm.temperature;
+  A.tau = S->prm.entropy_threshold;
+  A.lambda = S->prm.distance_penalty;
+  A.nseq = nb;
+  A.seq_rows = d_rows;
+  A.mask_pos = d_mpos;
+  A.caps = d_caps;
+  A.running = S->running;
+  A.running_idx = d_ridx;
+  A.H = dH;
+  A.argmax = dA;
+  A.selected = dS;
+  A.n_selected = dN;
+  const size_t nout = (size_t)3 * S->rows_cap + nb;
+  int* ho = S->h_out;
+  long global_live = 0;
+  if (S->sharded) {
+    WEDLM_TRY(sharded_select(ctx, S, A, nin, &global_live));
+  } else if (rr > 0) {
     WEDLM_CUDA_TRY(cudaMemcpyAsync(S->d_in, hi, (size_t)nin * 4, cudaMemcpyHostToDevice, st));
     S->h2d_bytes += nin * 4;
-    int* d_rows = S->d_in;
-    int* d_mpos = d_rows + nb + 1;
-    int* d_caps = d_mpos + rr;
-    int* d_ridx = d_caps + nb;
-    float* dH = reinterpret_cast<float*>(S->d_out);
-    int* dA = S->d_out + S->rows_cap;
-    int* dS = dA + S->rows_cap;
-    int* dN = dS + S->rows_cap;
-    EntropyArgs A;
     A.logits = S->logits;
-    A.dtype = m->dt;
-    A.rows = rr;
     A.V = m->vshard;
     A.ld = m->vshard;
-    A.temperature = S->prm.temperature;
-    A.tau = S->prm.entropy_threshold;
-    A.lambda = S->prm.distance_penalty;
-    A.nseq = nb;
-    A.seq_rows = d_rows;
-    A.mask_pos = d_mpos;
-    A.caps = d_caps;
-    A.running = S->running;
-    A.running_idx = d_ridx;
-    A.H = dH;
-    A.argmax = dA;
-    A.selected = dS;
-    A.n_selected = dN;
     EntropyPlan ep = plan_entropy(rr, m->vshard, m->dt, ctx->num_sms);
     WEDLM_TRY(ensure_entropy_scratch(ctx, rr, nb, (long)rr * ep.splits * 4));
     const int ph = prof_begin(ctx, st);
     WEDLM_TRY(run_entropy_select(A, ctx->ent, ctx->num_sms, st));
     prof_end(ctx, st, ph, WedlmProfiler::kEntropy, (double)rr * m->vshard * m->esz, 0, 1);
-    const size_t nout = (size_t)3 * S->rows_cap + nb;
-    int* ho = S->h_out;
     WEDLM_CUDA_TRY(cudaMemcpyAsync(ho, S->d_out, nout * 4, cudaMemcpyDeviceToHost, st));
     WEDLM_CUDA_TRY(cudaMemcpyAsync(ho + nout, ctx->dev_err, 4, cudaMemcpyDeviceToHost, st));
     S->d2h_bytes += (int64_t)(nout + 1) * 4;
     WEDLM_CUDA_TRY(cudaStreamSynchronize(st));
+  } else {
+    WEDLM_CUDA_TRY(cudaStreamSynchronize(st));
+  }
+  if (S->sharded || rr > 0) {
     prof_collect(ctx);
     if (ho[nout] != 0) {
       cudaMemsetAsync(ctx->dev_err, 0, 4, st);
       return Status::err(WEDLM_ERR_TIMEOUT, "a device-side wait gave up during the decode step");
     }
+  }
+  if (rr > 0) {
     const float* Hh = reinterpret_cast<const float*>(ho);
     const int* Ah = ho + S->rows_cap;
     const int* Sh = Ah + S->rows_cap;
@@ -319,8 +473,11 @@ Status session_step(wedlm_ctx* ctx, int* live_after) {
         }
       }
     }
-  } else {
-    WEDLM_CUDA_TRY(cudaStreamSynchronize(st));
+  }
+  if (S->sharded) {
+    // Every rank sees the same gathered header, so every rank stops after the same step.
+    *live_after = (int)std::min<long>(global_live, 1L << 30);
+    return Status::ok();
   }
   int live = 0;
   for (const SeqRun& R : S->runs)

@@ -499,12 +499,12 @@ entropy_partials_kernel(const T* __restrict__ logits, int V, long ld, int splits
 }
 
 __global__ void __launch_bounds__(kThreads)
-entropy_combine_kernel(const float* __restrict__ part, int nshards, int rows, const int* seq_rows,
-                       const int* mask_pos, const int* caps, float tau, float lambda,
-                       float* row_H, float* H, int* argmax, float* maxprob, int* selected,
-                       int* n_selected, float* running, const int* running_idx) {
+entropy_combine_kernel(const float* __restrict__ part, int nshards, long shard_stride,
+                       const int* seq_rows, const int* mask_pos, const int* caps, float tau,
+                       float lambda, float* row_H, float* H, int* argmax, float* maxprob,
+                       int* selected, int* n_selected, float* running, const int* running_idx) {
   const int b = blockIdx.x;
-  finalize_sequence(b, seq_rows[b], seq_rows[b + 1], part, 1, rows, nshards, tau, lambda,
+  finalize_sequence(b, seq_rows[b], seq_rows[b + 1], part, 1, shard_stride, nshards, tau, lambda,
                     mask_pos, caps, row_H, H, argmax, maxprob, selected, n_selected, running,
                     running_idx);
 }
@@ -608,12 +608,14 @@ Status run_entropy_partials(const EntropyArgs& A, const EntropyScratch& W, int v
 }
 
 Status run_entropy_combine(const float* partials, int nshards, const EntropyArgs& A,
-                           const EntropyScratch& W, cudaStream_t st) {
+                           const EntropyScratch& W, cudaStream_t st, long shard_stride) {
   WEDLM_CHECK_ARG(partials != nullptr && nshards >= 1, "bad partials");
   WEDLM_CHECK_ARG(A.nseq >= 1 && A.seq_rows && A.mask_pos && A.caps && A.selected && A.n_selected,
                   "seq_rows, mask_pos, caps, selected and n_selected are required");
   WEDLM_CHECK_ARG(A.rows <= W.row_capacity, "entropy scratch too small");
-  entropy_combine_kernel<<<A.nseq, kThreads, 0, st>>>(partials, nshards, A.rows, A.seq_rows,
+  if (shard_stride <= 0) shard_stride = A.rows;
+  WEDLM_CHECK_ARG(shard_stride >= A.rows, "shard stride shorter than the rows");
+  entropy_combine_kernel<<<A.nseq, kThreads, 0, st>>>(partials, nshards, shard_stride, A.seq_rows,
                                                       A.mask_pos, A.caps, A.tau, A.lambda, W.row_H,
                                                       A.H, A.argmax, A.maxprob, A.selected,
                                                       A.n_selected, A.running, A.running_idx);

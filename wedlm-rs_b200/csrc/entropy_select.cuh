@@ -48,7 +48,9 @@ Status run_entropy_select(const EntropyArgs& A, const EntropyScratch& W, int num
                           cudaStream_t st);
 Status run_entropy_partials(const EntropyArgs& A, const EntropyScratch& W, int vocab_offset,
                             float* out, int num_sms, cudaStream_t st);
+// Shard k's partial of row r is at partials + (k * shard_stride + r) * 4 (shard_stride in
+// rows; <= 0 means A.rows, i.e. [nshards, rows * 4] packed).
 Status run_entropy_combine(const float* partials, int nshards, const EntropyArgs& A,
-                           const EntropyScratch& W, cudaStream_t st);
+                           const EntropyScratch& W, cudaStream_t st, long shard_stride = 0);
 
 }  // namespace wedlm

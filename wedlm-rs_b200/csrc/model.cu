@@ -435,7 +435,7 @@ void model_destroy(wedlm_ctx* ctx) {
 // ---- forward --------------------------------------------------------------------------
 Status model_forward(wedlm_ctx* ctx, const std::vector<SeqSlice>& seqs, const int* tokens,
                      const int* positions, const int* rank, void* logits, int logits_dtype,
-                     int* n_logit_rows, cudaStream_t st) {
+                     int* n_logit_rows, cudaStream_t st, void* hidden_out) {
   ModelState* m = ctx->model;
   const int B = (int)seqs.size();
   WEDLM_CHECK_ARG(B >= 1 && B <= m->max_seqs, "bad number of sequences");
@@ -693,7 +693,7 @@ Status model_forward(wedlm_ctx* ctx, const std::vector<SeqSlice>& seqs, const in
     }
   }
   for (int b = 0; b < B; ++b) m->pending_rows[seqs[b].slot] = seqs[b].rows;
-  if (!logits || RL == 0) return Status::ok();
+  if ((!logits && !hidden_out) || RL == 0) return Status::ok();
 
   if (!tc) {
     const int ph = prof_begin(ctx, st);
@@ -702,23 +702,60 @@ Status model_forward(wedlm_ctx* ctx, const std::vector<SeqSlice>& seqs, const in
     WEDLM_TRY(sn);
   }
   const void* xl = m->xn;
-  if (RL != R) {
+  if (RL != R || hidden_out) {
+    void* dst = hidden_out ? hidden_out : m->xl;
     ctx->launches += 1;
     if (m->dt == WEDLM_BF16)
       WEDLM_CUDA_TRY(launch_pdl(gather_rows_kernel<__nv_bfloat16>, dim3(RL), dim3(256), 0, st,
                                 (const __nv_bfloat16*)m->xn, (long)H, (const int*)(d + o_lsrc),
-                                (__nv_bfloat16*)m->xl, (long)H, m->H));
+                                (__nv_bfloat16*)dst, (long)H, m->H));
     else
       WEDLM_CUDA_TRY(launch_pdl(gather_rows_kernel<float>, dim3(RL), dim3(256), 0, st,
                                 (const float*)m->xn, (long)H, (const int*)(d + o_lsrc),
-                                (float*)m->xl, (long)H, m->H));
-    xl = m->xl;
+                                (float*)dst, (long)H, m->H));
+    xl = dst;
   }
-  const int lepi = (logits_dtype == WEDLM_F32 && m->dt == WEDLM_BF16) ? EPI_STORE_F32 : EPI_STORE_BF16;
-  WEDLM_TRY(gemm(xl, H, m->lm_head, nullptr, m->vshard, m->H, lepi, logits, m->vshard, nullptr, 0,
-                 RL, nullptr));
+  if (hidden_out) return Status::ok();
   (void)es;
-  return Status::ok();
+  return model_lm_head(ctx, xl, H, RL, logits, logits_dtype, st);
+}
+
+Status model_lm_head(wedlm_ctx* ctx, const void* x, long ldx, int M, void* logits,
+                     int logits_dtype, cudaStream_t st) {
+  ModelState* m = ctx->model;
+  WEDLM_CHECK_ARG(logits_dtype == m->dt || logits_dtype == WEDLM_F32,
+                  "logits dtype must be the model dtype or F32");
+  WEDLM_CHECK_ARG(M >= 0 && x && logits, "bad LM-head rows");
+  if (M == 0) return Status::ok();
+  const bool tc = m->dt == WEDLM_BF16;
+  const int es = m->esz;
+  GemmArgs g;
+  g.X = x;
+  g.ldx = ldx;
+  g.W = m->lm_head;
+  g.ldw = m->H;
+  g.M = M;
+  g.N = m->vshard;
+  g.K = m->H;
+  g.epi = (logits_dtype == WEDLM_F32 && tc) ? EPI_STORE_F32 : EPI_STORE_BF16;
+  g.out = logits;
+  g.ldo = m->vshard;
+  const double bytes = (double)m->vshard * m->H * es + (double)M * m->H * es +
+                       (double)M * m->vshard * (g.epi == EPI_STORE_F32 ? 4 : es);
+  const double flops = 2.0 * M * m->vshard * m->H;
+  if (!tc) {
+    const int ph = prof_begin(ctx, st);
+    Status s = run_gemm_f32(g, st);
+    prof_end(ctx, st, ph, WedlmProfiler::kGemm, bytes, flops, 1);
+    return s;
+  }
+  g.w_packed = true;
+  GemmPlan gp = plan_gemm_tc(M, m->vshard, m->H, false, ctx->num_sms);
+  WEDLM_TRY(ensure_gemm_scratch(ctx, gp.ws_floats, gp.counters));
+  const int ph = prof_begin(ctx, st);
+  Status s = run_gemm_tc(g, gp, ctx->gemm_ws, ctx->gemm_counters, ctx->dev_err, st);
+  prof_end(ctx, st, ph, WedlmProfiler::kGemm, bytes, flops, gp.grid > 1 ? 2 : 1);
+  return s;
 }
 
 }  // namespace wedlm

@@ -81,8 +81,15 @@ void model_destroy(wedlm_ctx* ctx);
 // rows (sequence-major).  Writes the window K/V at each slot's committed length (not
 // committed) and, when logits != NULL, the logits of every sequence's rows
 // [logit_begin, rows) densely to logits ([n, vshard], dtype logits_dtype).
+// When hidden_out != NULL the LM head is not run: the final-normed hidden rows of the
+// logit rows are written densely to hidden_out ([n, H], model dtype) instead.
 Status model_forward(wedlm_ctx* ctx, const std::vector<SeqSlice>& seqs, const int* tokens,
                      const int* positions, const int* rank, void* logits, int logits_dtype,
-                     int* n_logit_rows, cudaStream_t st);
+                     int* n_logit_rows, cudaStream_t st, void* hidden_out = nullptr);
+
+// The LM head alone (this context's vocabulary shard) over M final-normed hidden rows
+// x ([M, ldx], model dtype, device): logits [M, vshard] of dtype logits_dtype.
+Status model_lm_head(wedlm_ctx* ctx, const void* x, long ldx, int M, void* logits,
+                     int logits_dtype, cudaStream_t st);
 
 }  // namespace wedlm

@@ -5,4 +5,4 @@ reference (``WeDLMForCausalLM``, ``WeDLMDecoder``, ``SamplingParams``); every co
 call goes through ``libwedlm_b200.so``.
 """
 from ._lib import BF16, F16, F32, WedlmError, lib  # noqa: F401
-from .context import Context, SamplingParams, ModelConfig  # noqa: F401
+from .context import Context, SamplingParams, ModelConfig, comm_unique_id  # noqa: F401

@@ -87,6 +87,9 @@ _PROTOS = {
     "wedlm_decode_io_bytes": (C.c_int, [P, C.POINTER(C.c_int64), C.POINTER(C.c_int64),
                                         C.POINTER(C.c_int64)]),
     "wedlm_decode_end": (C.c_int, [P]),
+    "wedlm_comm_unique_id": (C.c_int, [P, C.c_int]),
+    "wedlm_comm_init": (C.c_int, [P, P, C.c_int, C.c_int, C.c_int]),
+    "wedlm_comm_destroy": (C.c_int, [P]),
     # kernel-level entry points (include/wedlm_b200_kernels.h)
     "wedlm_kernel_gemm": (C.c_int, [P, P, C.c_int64, P, P, C.c_int64, C.c_int, C.c_int, C.c_int,
                                     C.c_int, C.c_int, C.c_int, P, C.c_int64, P, C.c_int64, P]),

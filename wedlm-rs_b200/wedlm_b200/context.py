@@ -417,6 +417,16 @@ class Context:
         return [out[b, :n[b]].tolist() for b in range(nseq)], steps
 
     # ---- step-wise streaming decode session ----------------------------------------------
+    def comm_init(self, unique_id: bytes, rank: int, nranks: int, timeout_ms: int = 30000) -> None:
+        """Join an NCCL communicator (collective over ``nranks`` processes, one GPU
+        each).  The ranks' vocab shards must tile [0, V) in rank order; the decode loops
+        then run the LM head and the entropy pass vocabulary-sharded."""
+        buf = C.create_string_buffer(bytes(unique_id), 128)
+        check(lib().wedlm_comm_init(self.h, buf, rank, nranks, timeout_ms), self.h)
+
+    def comm_destroy(self) -> None:
+        check(lib().wedlm_comm_destroy(self.h), self.h)
+
     def decode_begin(self, seq_ids, prompts, max_new_tokens: int, window_size: int,
                      params: SamplingParams, stream=None) -> None:
         import numpy as np
@@ -470,3 +480,10 @@ class Context:
         v = C.c_int64()
         check(lib().wedlm_launch_count(self.h, C.byref(v)), self.h)
         return v.value
+
+
+def comm_unique_id() -> bytes:
+    """A fresh 128-byte NCCL unique id (make it on one rank, hand it to every rank)."""
+    buf = C.create_string_buffer(128)
+    check(lib().wedlm_comm_unique_id(buf, 128))
+    return buf.raw
