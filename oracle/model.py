@@ -253,11 +253,14 @@ class OracleModel:
 
     # -- public API mirroring causal_lm.rs --------------------------------------
     def forward_with_positions(self, input_ids, positions, kv_caches=None, rank=None,
-                               logits_rows: Optional[slice] = None, round_logits: bool = True):
+                               logits_rows: Optional[slice] = None, round_logits: bool = True,
+                               return_hidden: bool = False):
         """``WeDLMForCausalLM::forward_with_positions`` (``causal_lm.rs:68-79``).
 
         Returns ``(logits [S or rows, V], new_caches)``.  ``new_caches`` holds the
         concatenated ``cache ++ block`` K/V per layer, as the reference returns.
+        ``return_hidden`` returns the final-normed hidden rows (the LM head's input,
+        ``causal_lm.rs:77``) in place of the logits.
         """
         ids = np.asarray(input_ids, dtype=np.int64).reshape(-1)
         pos = np.asarray(positions, dtype=np.int64).reshape(-1)
@@ -274,6 +277,8 @@ class OracleModel:
         h = self._r(rms_norm(h, self.w["model.norm.weight"], self.cfg.rms_norm_eps))
         if logits_rows is not None:
             h = h[logits_rows]
+        if return_hidden:
+            return h, new
         logits = np.matmul(h, self.w["lm_head.weight"].T, dtype=np.float32)
         if round_logits:
             logits = self._r(logits)
