@@ -214,6 +214,14 @@ WEDLM_API int wedlm_entropy_combine(wedlm_ctx* ctx, const float* partials, int n
                           int32_t* argmax, float* maxprob, int32_t* selected,
                           int32_t* n_selected, void* stream);
 
+/* Seed of the T > 0 draws of the decode loops (default 0).  The reference samples with
+ * the unseeded thread_rng (src/decoding/sampler.rs:180); here the draw of mask row i of
+ * sequence b (its index in the call) at step n (1-based) is SplitMix64 chained over
+ * (seed, b, n, i), so a seeded run is reproducible.  With T > 0 the selected rows are
+ * sampled from softmax(logits / T), by nucleus when top_p < 1 (sampler.rs:306-351);
+ * the entropies and the selection are those of the same scaled distribution. */
+WEDLM_API int wedlm_set_sampling_seed(wedlm_ctx* ctx, uint64_t seed);
+
 /* ---- multi-GPU: vocabulary-sharded LM head and entropy pass ------------------------- */
 
 /* The reference runs on one device and has no collective; these replace nothing in it.

@@ -59,6 +59,18 @@ WEDLM_API int wedlm_kernel_attention_prepare(wedlm_ctx* ctx, const void* q, cons
                                              const int32_t* rank, void* stream);
 WEDLM_API int wedlm_kernel_attention_run(wedlm_ctx* ctx, void* out, void* stream);
 
+/* The T > 0 branches of sample_from_probs_at_indices (src/decoding/sampler.rs:160-200,
+ * 306-351) on caller buffers, with the draw given: row r of softmax(logits / T) is
+ * sampled with u[r] in [0, 1) (device f32 [rows]) and its token written to tokens[r]
+ * (device int32 [rows]).  top_p >= 1: the first token whose running probability sum
+ * exceeds u (sample_from_probs); top_p < 1: the nucleus, i.e. the most probable tokens
+ * (ties in index order) until their sum reaches top_p, renormalised, then the same rule
+ * in that order (sample_nucleus).  Sums are exact in 2^-40 fixed point, so a row and a
+ * draw always give the same token.  temperature > 0. */
+WEDLM_API int wedlm_kernel_sample(wedlm_ctx* ctx, const void* logits, int dtype, int rows, int V,
+                                  int ld, float temperature, float top_p, const float* u,
+                                  int32_t* tokens, void* stream);
+
 /* Synchronises `stream`, then reports (and clears) a device-side wait that gave up
  * inside a kernel since the last check: WEDLM_ERR_TIMEOUT, else WEDLM_OK. */
 WEDLM_API int wedlm_check_device_error(wedlm_ctx* ctx, void* stream);

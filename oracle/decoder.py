@@ -18,7 +18,8 @@ from typing import List, Optional, Sequence
 import numpy as np
 
 from .sampler import (SamplingParams, compute_entropies_with_probs, effective_cap,
-                      greedy_argmax_last, select_by_entropy_with_distance,
+                      greedy_argmax_last, sample_from_probs, sample_nucleus,
+                      sampling_uniform, scale_logits, select_by_entropy_with_distance,
                       update_running_entropy)
 
 ENTROPY_SOFT_THRESHOLD = 8.0   # wedlm.rs:29
@@ -97,13 +98,17 @@ class StepTrace:
 class OracleDecoder:
     """``WeDLMDecoder`` restated; the cache is a Python list of per-layer (K, V)."""
 
-    def __init__(self, model, mask_token_id: int, eos_token_id: int):
+    def __init__(self, model, mask_token_id: int, eos_token_id: int, seed: int = 0,
+                 seq_index: int = 0):
         self.model = model
         self.mask = int(mask_token_id)
         self.eos = int(eos_token_id)
         self.cache = None
         self.cache_len = 0
         self.trace: List[StepTrace] = []
+        # T > 0: the seeded draws of the device sampler (``sampling_uniform``)
+        self.seed = int(seed)
+        self.seq_index = int(seq_index)
 
     def _truncate(self, new_len: int):
         """``truncate_cache`` (``wedlm.rs:308-323``)."""
@@ -112,10 +117,23 @@ class OracleDecoder:
         self.cache = [(k[:, :new_len], v[:, :new_len]) for (k, v) in self.cache]
         self.cache_len = new_len
 
-    def _sample(self, probs, selected, temperature):
-        if temperature != 0.0:
-            raise NotImplementedError("only T = 0 is reproducible (unseeded RNG in sampler.rs:180)")
-        return [greedy_argmax_last(probs[i]) for i in selected]
+    def _sample(self, probs, selected, params, step: int, logits=None):
+        """``sample_from_probs_at_indices`` (``sampler.rs:160-200``).  T > 0 draws
+        ``sampling_uniform(seed, seq_index, step, row)`` in place of the reference's
+        unseeded ``thread_rng``, over float64 probabilities of ``logits`` (the mask rows)."""
+        if params.temperature == 0.0:
+            return [greedy_argmax_last(probs[i]) for i in selected]
+        x = scale_logits(np.asarray(logits), params.temperature).astype(np.float64)
+        e = np.exp(x - x.max(axis=-1, keepdims=True))
+        probs = e / e.sum(axis=-1, keepdims=True)
+        out = []
+        for i in selected:
+            u = sampling_uniform(self.seed, self.seq_index, step, i)
+            if params.top_p >= 1.0:
+                out.append(sample_from_probs(probs[i], u))
+            else:
+                out.append(sample_nucleus(probs[i], params.top_p, u))
+        return out
 
     def generate_streaming(self, prompt_ids: Sequence[int], max_new_tokens: int,
                            window_size: int, params: SamplingParams):
@@ -182,7 +200,7 @@ class OracleDecoder:
             eff = effective_cap(running, params.entropy_threshold, params.max_tokens_per_step)
             sel = select_by_entropy_with_distance(H, mask_logical, params.entropy_threshold,
                                                   params.distance_penalty, eff)
-            toks = self._sample(probs, sel, params.temperature)
+            toks = self._sample(probs, sel, params, stats.steps, mlog)
             tr.entropies, tr.effective_max, tr.selected, tr.sampled = list(H), eff, sel, toks
             for i, s in enumerate(sel):
                 post = max(mask_logical[s] - n_commit, 0)
@@ -215,13 +233,14 @@ class OracleDecoder:
             ro = compute_block_reorder(block, mask_pos, P)
             logits, _ = self.model.forward_with_positions(ro.reordered_block, ro.positions, self.cache)
             nf, nm = ro.num_filled, len(mask_pos)
-            H, probs = compute_entropies_with_probs(np.asarray(logits)[nf:nf + nm], params.temperature)
+            mlog = np.asarray(logits)[nf:nf + nm]
+            H, probs = compute_entropies_with_probs(mlog, params.temperature)
             orig = [ro.block_permutation[i] for i in range(nf, block_size)]
             sel = select_by_entropy_with_distance(H, orig, params.entropy_threshold,
                                                   params.distance_penalty, params.max_tokens_per_step)
             if not sel:
                 break
-            toks = self._sample(probs, sel, params.temperature)
+            toks = self._sample(probs, sel, params, stats.steps, mlog)
             fill = []
             for i, s in enumerate(sel):
                 fill.append((ro.block_permutation[nf + s], toks[i]))

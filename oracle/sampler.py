@@ -2,7 +2,9 @@
 
 * ``SamplingParams`` and presets      ``src/decoding/sampler.rs:12-44``, ``src/bin/cli.rs:113-137``
 * ``compute_entropies_with_probs``    ``src/decoding/sampler.rs:125-154``
-* ``sample_from_probs_at_indices``    ``src/decoding/sampler.rs:160-200`` (T = 0 branch)
+* ``sample_from_probs_at_indices``    ``src/decoding/sampler.rs:160-200`` (T = 0 branch; the
+  T > 0 branches ``sample_from_probs`` / ``sample_nucleus``, ``sampler.rs:306-351``, with the
+  uniform draw passed in, since the reference's ``thread_rng`` is unseeded)
 * ``select_by_entropy_with_distance`` ``src/decoding/sampler.rs:446-493``
 * streaming dynamic cap (entropy EMA) ``src/decoding/wedlm.rs:517-535``
 """
@@ -107,6 +109,57 @@ def combine_partials(parts):
         am = np.where(take, p[3], am)
         best = np.where(take, p[0], best)
     return H, am.astype(np.int32), (1.0 / S).astype(np.float32)
+
+
+_MASK64 = (1 << 64) - 1
+
+
+def splitmix64(x: int) -> int:
+    """The SplitMix64 output function (Steele, Lea and Flood, OOPSLA 2014)."""
+    x = (x + 0x9E3779B97F4A7C15) & _MASK64
+    x = ((x ^ (x >> 30)) * 0xBF58476D1CE4E5B9) & _MASK64
+    x = ((x ^ (x >> 27)) * 0x94D049BB133111EB) & _MASK64
+    return x ^ (x >> 31)
+
+
+def sampling_uniform(seed: int, seq: int, step: int, row: int) -> np.float32:
+    """The seeded draw of the device sampler for mask row ``row`` of sequence ``seq`` at
+    decode step ``step`` (1-based): a 24-bit uniform in [0, 1), the precision of the
+    reference's ``rng.gen::<f32>()``."""
+    h = splitmix64(seed & _MASK64)
+    h = splitmix64(h ^ (seq & _MASK64))
+    h = splitmix64(h ^ (step & _MASK64))
+    h = splitmix64(h ^ (row & _MASK64))
+    return np.float32((h >> 40) * 2.0 ** -24)
+
+
+def sample_from_probs(probs: np.ndarray, r: float) -> int:
+    """``sample_from_probs`` (``sampler.rs:306-317``) with the draw ``r`` given: the first
+    index whose running sum exceeds r; the last index when rounding leaves none.  The
+    running sums are float64 here; the reference's f32 running sum differs from the exact
+    one by O(V * 2^-24)."""
+    c = np.cumsum(np.asarray(probs, np.float64))
+    hit = np.nonzero(float(r) < c)[0]
+    return int(hit[0]) if hit.size else int(len(c) - 1)
+
+
+def sample_nucleus(probs: np.ndarray, top_p: float, r: float) -> int:
+    """``sample_nucleus`` (``sampler.rs:320-351``) with the draw ``r`` given: probabilities
+    sorted descending (stable, so ties keep index order), the smallest prefix whose running
+    sum reaches top_p, renormalised, and the first member whose running sum exceeds
+    r * total; the most probable token when rounding leaves none.  Sums in float64, as in
+    ``sample_from_probs``."""
+    p = np.asarray(probs, np.float64)
+    order = np.argsort(-p, kind="stable")
+    ps = p[order]
+    c = np.cumsum(ps)
+    reach = np.nonzero(c >= float(np.float32(top_p)))[0]
+    cut = int(reach[0]) + 1 if reach.size else len(ps)
+    run = c[:cut]
+    total = run[-1]
+    target = float(r) * total
+    hit = np.nonzero(target < run)[0]
+    return int(order[hit[0]]) if hit.size else int(order[0])
 
 
 def greedy_argmax_last(probs_row: np.ndarray) -> int:

@@ -230,3 +230,28 @@ def test_c_restatement_matches_numpy():
     rf = cbind.entropy_select(x, "f32", 0.5, 0.8, 0.05, [0, 24], mask_pos, [8])
     Hf, amf, _ = row_stats(x, 0.5)
     assert np.abs(rf["H"] - Hf).max() < 2e-3 and (rf["tokens"] == amf).all()
+
+
+def test_seeded_sampling_restatement():
+    """sample_from_probs / sample_nucleus (sampler.rs:306-351) with the draw given, and
+    the SplitMix64 draws: known answers, the nucleus bound, and frequencies that follow
+    the probabilities."""
+    from oracle.sampler import sample_from_probs, sample_nucleus, sampling_uniform, splitmix64
+    # SplitMix64 reference outputs for state 0 (the generator's first three outputs)
+    assert splitmix64(0) == 0xE220A8397B1DCDAF
+    p = np.array([0.1, 0.4, 0.2, 0.3], np.float32)
+    assert [sample_from_probs(p, r) for r in (0.05, 0.12, 0.49, 0.51, 0.71, 0.99)] == [0, 1, 1, 2, 3, 3]
+    # nucleus at 0.6: tokens 1 (0.4) and 3 (0.3), renormalised over 0.7
+    assert [sample_nucleus(p, 0.6, r) for r in (0.0, 0.5, 0.57, 0.58, 0.99)] == [1, 1, 1, 3, 3]
+    # ties keep index order: 2 and 3 tie, 2 comes first
+    q = np.array([0.1, 0.3, 0.3, 0.3], np.float32)
+    assert sample_nucleus(q, 0.5, 0.2) == 1 and sample_nucleus(q, 0.5, 0.8) == 2
+    u = np.array([sampling_uniform(7, 0, s, i) for s in range(1, 41) for i in range(50)])
+    assert u.min() >= 0.0 and u.max() < 1.0 and abs(u.mean() - 0.5) < 0.02
+    assert len(set(u.tolist())) > 1990
+    probs = np.array([0.05, 0.5, 0.15, 0.3])
+    counts = np.bincount([sample_from_probs(probs, x) for x in u], minlength=4) / len(u)
+    assert np.abs(counts - probs).max() < 0.02
+    nuc = [sample_nucleus(probs, 0.7, x) for x in u]
+    assert set(nuc) == {1, 3}
+    assert abs(np.mean(np.array(nuc) == 1) - 0.5 / 0.8) < 0.03

@@ -7,6 +7,7 @@
 #include "comm.h"
 #include "context.h"
 #include "model.h"
+#include "sample.cuh"
 #include "gemm.h"
 #include "../../include/wedlm_b200_kernels.h"
 
@@ -383,5 +384,32 @@ extern "C" int wedlm_kernel_pack_weight(wedlm_ctx* ctx, const void* W, int64_t l
   if (!W || !packed || N <= 0 || K <= 0 || K % 64 != 0 || (uintptr_t)packed % 16 != 0)
     return ctx->fail(Status::err(WEDLM_ERR_INVALID_ARG, "bad pack arguments"));
   Status s = wedlm::pack_weight(W, ld, 0, N, K, packed, (cudaStream_t)stream);
+  return s.good() ? WEDLM_OK : ctx->fail(s);
+}
+
+extern "C" int wedlm_set_sampling_seed(wedlm_ctx* ctx, uint64_t seed) {
+  if (!ctx) return WEDLM_ERR_INVALID_ARG;
+  ctx->sample_seed = seed;
+  return WEDLM_OK;
+}
+
+extern "C" int wedlm_kernel_sample(wedlm_ctx* ctx, const void* logits, int dtype, int rows, int V,
+                                   int ld, float temperature, float top_p, const float* u,
+                                   int32_t* tokens, void* stream) {
+  if (!ctx) return WEDLM_ERR_INVALID_ARG;
+  if (int rc = set_device(ctx)) return rc;
+  if (!u) return ctx->fail(Status::err(WEDLM_ERR_INVALID_ARG, "u is NULL"));
+  wedlm::SampleArgs a;
+  a.logits = logits;
+  a.dtype = dtype;
+  a.rows = rows;
+  a.V = V;
+  a.ld = ld;
+  a.temperature = temperature;
+  a.top_p = top_p;
+  a.u = u;
+  a.tokens = tokens;
+  Status s = wedlm::run_sample(a, (cudaStream_t)stream);
+  if (s.good()) ctx->launches += rows > 0 ? 1 : 0;
   return s.good() ? WEDLM_OK : ctx->fail(s);
 }

@@ -6,11 +6,13 @@
 // forwarded once more at sequential positions to enter the cache.  generate_with_stats
 // adapts the block size to the block's entropies and refreshes the cache.
 #include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <vector>
 
 #include "entropy_select.cuh"
 #include "model.h"
+#include "sample.cuh"
 
 namespace wedlm {
 namespace {
@@ -34,7 +36,8 @@ struct BlockBuffers {
   Status alloc(const ModelState* m, int block) {
     cap = block;
     WEDLM_CUDA_TRY(cudaMalloc(&logits, (size_t)block * m->vshard * m->esz + 256));
-    const size_t ints = 3 + (size_t)block + 3 * (size_t)block + 2;
+    // + [sequence key, step] of the T > 0 draws after the outputs
+    const size_t ints = 3 + (size_t)block + 3 * (size_t)block + 1 + 2;
     WEDLM_CUDA_TRY(cudaMalloc(&d_io, ints * 4));
     WEDLM_CUDA_TRY(cudaMallocHost(&h_io, ints * 4));
     return Status::ok();
@@ -130,6 +133,32 @@ Status generate_block(wedlm_ctx* ctx, int slot, const int32_t* prefix, int n_pre
     EntropyPlan ep = plan_entropy(nm, m->vshard, m->dt, ctx->num_sms);
     WEDLM_TRY(ensure_entropy_scratch(ctx, nm, 1, (long)nm * ep.splits * 4));
     WEDLM_TRY(run_entropy_select(A, ctx->ent, ctx->num_sms, st));
+    if (prm.temperature > 0.f) {
+      // T > 0: the selected rows are drawn (sample_from_probs / sample_nucleus) in place
+      // of their argmax, keyed by (seed, 0, step, mask row)
+      int* hkv = B.h_io + 4 + 4 * B.cap;
+      int* dkv = B.d_io + 4 + 4 * B.cap;
+      hkv[0] = 0;
+      hkv[1] = (int)s.steps;
+      WEDLM_CUDA_TRY(cudaMemcpyAsync(dkv, hkv, 2 * sizeof(int), cudaMemcpyHostToDevice, st));
+      SampleArgs sa;
+      sa.logits = B.logits;
+      sa.dtype = m->dt;
+      sa.rows = nm;
+      sa.V = m->vshard;
+      sa.ld = m->vshard;
+      sa.temperature = prm.temperature;
+      sa.top_p = prm.top_p;
+      sa.seed = ctx->sample_seed;
+      sa.nseq = 1;
+      sa.seq_rows = A.seq_rows;
+      sa.selected = A.selected;
+      sa.n_selected = A.n_selected;
+      sa.seq_key = dkv;
+      sa.seq_step = dkv + 1;
+      sa.tokens = A.argmax;
+      WEDLM_TRY(run_sample(sa, st));
+    }
     int* ho = B.h_io + 3 + B.cap;
     WEDLM_CUDA_TRY(cudaMemcpyAsync(ho, dout, (size_t)(3 * B.cap + 1) * 4, cudaMemcpyDeviceToHost, st));
     WEDLM_CUDA_TRY(cudaStreamSynchronize(st));
@@ -254,9 +283,9 @@ Status check_block_args(wedlm_ctx* ctx, int seq, int block_size, const wedlm_sam
   WEDLM_CHECK_ARG(block_size >= 1 && block_size <= m->cfg.max_block_tokens,
                   "block_size must be 1 .. max_block_tokens");
   WEDLM_CHECK_ARG(prm != nullptr, "params is NULL");
-  WEDLM_CHECK_ARG(prm->temperature == 0.f,
-                  "only temperature 0 (greedy) is supported: the reference samples with an "
-                  "unseeded RNG at T > 0");
+  WEDLM_CHECK_ARG(prm->temperature >= 0.f && std::isfinite(prm->temperature),
+                  "temperature must be >= 0");
+  WEDLM_CHECK_ARG(prm->temperature == 0.f || prm->top_p > 0.f, "top_p must be > 0");
   return Status::ok();
 }
 

@@ -62,6 +62,8 @@ struct wedlm_ctx {
   wedlm::AttnKernelScratch* att = nullptr;
   // NCCL communicator of the vocabulary-sharded decode (comm.cu); NULL on one GPU
   wedlm::Comm* comm = nullptr;
+  // seed of the T > 0 draws (sample.cu)
+  unsigned long long sample_seed = 0;
 
   int fail(const wedlm::Status& s) {
     last_error = s.msg;

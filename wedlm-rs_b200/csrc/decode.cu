@@ -24,9 +24,12 @@
 #include <cstring>
 #include <vector>
 
+#include <cmath>
+
 #include "comm.h"
 #include "entropy_select.cuh"
 #include "model.h"
+#include "sample.cuh"
 
 namespace wedlm {
 
@@ -145,9 +148,11 @@ Status session_begin(wedlm_ctx* ctx, const std::vector<int>& slots, const int32_
   }
   WEDLM_CHECK_ARG(n_prompt >= 1 && max_new >= 0 && window >= 1, "bad lengths");
   WEDLM_CHECK_ARG(window <= m->cfg.max_block_tokens, "window larger than max_block_tokens");
-  WEDLM_CHECK_ARG(prm.temperature == 0.f,
-                  "only temperature 0 (greedy) is supported: the reference samples with an "
-                  "unseeded RNG at T > 0");
+  WEDLM_CHECK_ARG(prm.temperature >= 0.f && std::isfinite(prm.temperature),
+                  "temperature must be >= 0");
+  WEDLM_CHECK_ARG(prm.temperature == 0.f || prm.top_p > 0.f, "top_p must be > 0");
+  WEDLM_CHECK_ARG(prm.temperature == 0.f || !ctx->comm,
+                  "T > 0 sampling needs the whole vocabulary on the context (no communicator)");
   WEDLM_CHECK_ARG(n_prompt + max_new + window <= m->max_ctx, "prompt + generation exceed max_ctx");
   if (!ctx->comm && m->vshard != m->V)
     return Status::err(WEDLM_ERR_STATE,
@@ -195,7 +200,7 @@ Status session_begin(wedlm_ctx* ctx, const std::vector<int>& slots, const int32_
   S->rows_cap = B * window;
   S->nseq_cap = B;
   const size_t lbytes = ((size_t)S->rows_cap * m->vshard * m->esz + 255) / 256 * 256;
-  const size_t in_ints = (size_t)3 * B + 1 + S->rows_cap + 4;  // + the sharded step's header
+  const size_t in_ints = (size_t)4 * B + 1 + S->rows_cap + 4;  // + the sharded step's header
   const size_t out_ints = (size_t)3 * S->rows_cap + B;
   const int nranks = ctx->comm ? comm_size(ctx->comm) : 1;
   WEDLM_CUDA_TRY(cudaMalloc(&S->block, lbytes + (in_ints + B + out_ints) * 4 + 1024));
@@ -392,16 +397,19 @@ Status session_step(wedlm_ctx* ctx, int* live_after) {
   }
   h_rows[nb] = rr;
   int* h_caps = h_mpos + rr;       // [nb]
-  int* h_ridx = h_caps + nb;       // [nb] running-entropy slot of each call sequence
+  int* h_ridx = h_caps + nb;       // [nb] running-entropy slot (session index) of each sequence
+  int* h_step = h_ridx + nb;       // [nb] its step number (key of the T > 0 draws)
   for (int k = 0; k < nb; ++k) {
     h_caps[k] = S->prm.max_tokens_per_step;
     h_ridx[k] = S->live[k];
+    h_step[k] = (int)S->runs[S->live[k]].st.steps;
   }
-  const int nin = nb + 1 + rr + 2 * nb;
+  const int nin = nb + 1 + rr + 3 * nb;
   int* d_rows = S->d_in;
   int* d_mpos = d_rows + nb + 1;
   int* d_caps = d_mpos + rr;
   int* d_ridx = d_caps + nb;
+  int* d_step = d_ridx + nb;
   float* dH = reinterpret_cast<float*>(S->d_out);
   int* dA = S->d_out + S->rows_cap;
   int* dS = dA + S->rows_cap;
@@ -438,6 +446,29 @@ Status session_step(wedlm_ctx* ctx, int* live_after) {
     const int ph = prof_begin(ctx, st);
     WEDLM_TRY(run_entropy_select(A, ctx->ent, ctx->num_sms, st));
     prof_end(ctx, st, ph, WedlmProfiler::kEntropy, (double)rr * m->vshard * m->esz, 0, 1);
+    if (S->prm.temperature > 0.f) {
+      // T > 0: the selected rows are drawn (sample_from_probs / sample_nucleus) in place
+      // of their argmax, keyed by (seed, session index, step, mask row)
+      SampleArgs sa;
+      sa.logits = S->logits;
+      sa.dtype = m->dt;
+      sa.rows = rr;
+      sa.V = m->vshard;
+      sa.ld = m->vshard;
+      sa.temperature = S->prm.temperature;
+      sa.top_p = S->prm.top_p;
+      sa.seed = ctx->sample_seed;
+      sa.nseq = nb;
+      sa.seq_rows = d_rows;
+      sa.selected = dS;
+      sa.n_selected = dN;
+      sa.seq_key = d_ridx;
+      sa.seq_step = d_step;
+      sa.tokens = dA;
+      const int ps = prof_begin(ctx, st);
+      WEDLM_TRY(run_sample(sa, st));
+      prof_end(ctx, st, ps, WedlmProfiler::kEntropy, 0, 0, 1);
+    }
     WEDLM_CUDA_TRY(cudaMemcpyAsync(ho, S->d_out, nout * 4, cudaMemcpyDeviceToHost, st));
     WEDLM_CUDA_TRY(cudaMemcpyAsync(ho + nout, ctx->dev_err, 4, cudaMemcpyDeviceToHost, st));
     S->d2h_bytes += (int64_t)(nout + 1) * 4;

@@ -87,6 +87,9 @@ _PROTOS = {
     "wedlm_decode_io_bytes": (C.c_int, [P, C.POINTER(C.c_int64), C.POINTER(C.c_int64),
                                         C.POINTER(C.c_int64)]),
     "wedlm_decode_end": (C.c_int, [P]),
+    "wedlm_set_sampling_seed": (C.c_int, [P, C.c_uint64]),
+    "wedlm_kernel_sample": (C.c_int, [P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float,
+                                      C.c_float, P, P, P]),
     "wedlm_comm_unique_id": (C.c_int, [P, C.c_int]),
     "wedlm_comm_init": (C.c_int, [P, P, C.c_int, C.c_int, C.c_int]),
     "wedlm_comm_destroy": (C.c_int, [P]),

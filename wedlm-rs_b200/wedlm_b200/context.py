@@ -172,6 +172,23 @@ class Context:
         check(rc, self.h)
         return out
 
+    def sample(self, logits, temperature: float, top_p: float, u, out=None, stream=None):
+        """T > 0 draw of every row of ``logits`` (CUDA ``[rows, V]``) with the uniforms
+        ``u`` (CUDA f32 ``[rows]``): multinomial, or nucleus when ``top_p < 1``."""
+        import torch
+        rows, V = logits.shape[0], logits.shape[1]
+        dt = BF16 if logits.dtype == torch.bfloat16 else F32
+        if out is None:
+            out = torch.empty(rows, dtype=torch.int32, device=logits.device)
+        check(lib().wedlm_kernel_sample(self.h, ptr(logits), dt, rows, V, logits.stride(0),
+                                        temperature, top_p, ptr(u), ptr(out), stream_ptr(stream)),
+              self.h)
+        return out
+
+    def set_sampling_seed(self, seed: int) -> None:
+        """Seed of the T > 0 draws of the decode loops."""
+        check(lib().wedlm_set_sampling_seed(self.h, seed & ((1 << 64) - 1)), self.h)
+
     def entropy_combine(self, partials, tau: float, lam: float, seq_rows, mask_pos, caps,
                         stream=None) -> dict:
         """``partials``: CUDA f32 ``[nshards, rows, 4]``."""
