@@ -648,9 +648,16 @@ PartialSet partial_set(const GemmPlan& g, const float* slots, bool dual) {
 
 GemmPlan plan_gemm_tc(int M, int N, int K, bool dual, int num_sms) {
   GemmPlan g;
+  // Many token rows (prefill chunks, batched serving): the GEMM is tensor-bound and its
+  // operands stream from L2.  Each unit then takes 256 token rows and two weight tiles
+  // (or gate and up), 512 accumulator columns in one TMEM buffer: 131 flop per operand
+  // byte against 85 with one 128 x 256 tile, at the cost of the epilogue no longer
+  // overlapping the next unit's main loop.
+  bool wide = M >= 512;
+  if (const char* e = getenv("WEDLM_GEMM_WIDE")) wide = wide && atoi(e) != 0;
   int tt = ((M + 15) / 16) * 16;
-  if (tt > 256 || (dual && tt > 128)) {
-    const int cap = dual ? 128 : 256;
+  if (tt > 256 || (dual && !wide && tt > 128)) {
+    const int cap = (dual && !wide) ? 128 : 256;
     const int nt = (M + cap - 1) / cap;
     tt = ((M + nt - 1) / nt + 15) / 16 * 16;
   }
@@ -663,7 +670,7 @@ GemmPlan plan_gemm_tc(int M, int N, int K, bool dual, int num_sms) {
   // as the larger units double the split-K partials their consumers read).  Dual
   // (gate/up) already shares the activations between two matrices, and above 128 token
   // rows the accumulators of two tiles would not double-buffer in TMEM.
-  int nb = (!dual && g.tok_tile <= 128 && g.n_tiles >= 2) ? 2 : 1;
+  int nb = (!dual && (g.tok_tile <= 128 || wide) && g.n_tiles >= 2) ? 2 : 1;
   if (const char* e = getenv("WEDLM_GEMM_NB")) nb = atoi(e) == 1 ? 1 : nb;
   g.nb = nb;
   const int na = dual ? 2 : 1;
