@@ -459,15 +459,18 @@ GEMM_SHAPES_8B = [("qkv", 6144, 4096, 0), ("o_resid", 4096, 4096, 2), ("gate_up_
 def bench_gemm_shapes(args, rank, ws, local):
     """The decode-step GEMM shapes on their own through wedlm_kernel_gemm: each step
     runs every shape once; weights rotate over enough copies to exceed L2, so every
-    launch streams its weights from HBM.  Reports GB/s (algorithmic bytes) per shape."""
+    launch streams its weights from HBM.  At the decode's 96 rows the shapes are
+    HBM-bound and report GB/s (algorithmic bytes); with --gemm-rows >= 512 (the 6144 rows
+    of batched serving) they are tensor-bound and report TFLOP/s."""
     import torch
     from wedlm_b200 import Context
-    hbm, _, peak_kind = peaks()
+    hbm, tflops, peak_kind = peaks()
     ctx = Context(None, device=local)
-    M = 96
+    M = args.gemm_rows
+    tensor = M >= 512
     X = torch.randn(M, 12288, device="cuda").to(torch.bfloat16)
     res = {}
-    total_bytes, total_ms = 0.0, 0.0
+    total_bytes, total_flops, total_ms = 0.0, 0.0, 0.0
     only = set(args.gemm_only.split(",")) if args.gemm_only else None
     for name, N, K, epi in GEMM_SHAPES_8B:
         if only and name not in only:
@@ -509,23 +512,30 @@ def bench_gemm_shapes(args, rank, ws, local):
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / n
         byt = wbytes + M * K * 2 + M * N * 2 * (2 if epi == 2 else 1)
+        flo = 2.0 * nW * M * N * K
         res[name] = {"N": N, "K": K, "us": round(ms * 1e3, 2), "GBps": round(byt / ms / 1e6, 1),
-                     "frac": round(byt / ms / 1e6 / hbm, 4)}
+                     "TFLOPs": round(flo / ms / 1e9, 1),
+                     "frac": round(flo / ms / 1e9 / tflops, 4) if tensor else
+                             round(byt / ms / 1e6 / hbm, 4)}
         total_bytes += byt
+        total_flops += flo
         total_ms += ms
         del Ws
         torch.cuda.empty_cache()
     ctx.check_device_error()
     ctx.close()
-    achieved = total_bytes / total_ms / 1e6
-    return {"metric": METRIC, "value": round(achieved, 1), "unit": "GB/s", "n_gpus": ws,
+    if tensor:
+        achieved, unit, bound, peak = total_flops / total_ms / 1e9, "TFLOP/s", "tensor", tflops
+    else:
+        achieved, unit, bound, peak = total_bytes / total_ms / 1e6, "GB/s", "hbm", hbm
+    return {"metric": METRIC, "value": round(achieved, 1), "unit": unit, "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic", "config": {"workload": "gemm_shapes: the five projection GEMMs "
-                                                        "of one 8B decode step at M = 96", "shapes": res,
+                                                        f"of one 8B step at M = {M}", "shapes": res,
                                             "l2": "weights rotated over > 300 MB of copies"},
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
-                         "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / hbm, 4)}}
+            "roofline": {"bound": bound, "achieved": round(achieved, 1), "peak": peak,
+                         "peak_kind": peak_kind, "unit": unit, "frac": round(achieved / peak, 4)}}
 
 
 # ----------------------------------------------------------------------------------
@@ -1049,6 +1059,8 @@ def main():
                     choices=["decode_8b", "entropy_select", "gemm_shapes", "block_attention",
                              "serve_8b"])
     ap.add_argument("--gemm-only", default="", help="comma list of gemm_shapes names")
+    ap.add_argument("--gemm-rows", type=int, default=96,
+                    help="gemm_shapes: token rows (96 = one decode window; 6144 = serve_8b)")
     ap.add_argument("--profile-steps", type=int, default=10,
                     help="decode steps timed per kernel class after the headline region")
     ap.add_argument("--no-entropy", action="store_true",

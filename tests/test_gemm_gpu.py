@@ -37,7 +37,8 @@ def check_close(y, ref, rtol=2 ** -7):
 
 SHAPES = [(96, 6144, 4096), (96, 4096, 4096), (96, 4096, 12288), (96, 151936, 4096),
           (1, 1000, 128), (17, 384, 64), (200, 1280, 512), (300, 640, 256), (768, 2048, 1024),
-          (1000, 1280, 512), (1536, 4096, 4096)]
+          (1000, 1280, 512), (1536, 4096, 4096),
+          (6144, 4096, 1024), (6144, 6144, 512)]
 
 
 @pytest.mark.parametrize("M,N,K", SHAPES)
@@ -67,7 +68,7 @@ def test_store_f32(ctx, M, N, K):
 
 
 @pytest.mark.parametrize("M,N,K", [(96, 4096, 4096), (96, 4096, 12288), (50, 256, 768),
-                                   (1024, 4096, 4096)])
+                                   (1024, 4096, 4096), (6144, 4096, 512)])
 def test_residual(ctx, M, N, K):
     X = bf(rand(M, K, seed=5))
     W = bf(rand(N, K, scale=K ** -0.5, seed=6))
@@ -80,7 +81,7 @@ def test_residual(ctx, M, N, K):
 
 
 @pytest.mark.parametrize("M,N,K", [(96, 12288, 4096), (20, 768, 256), (300, 512, 512),
-                                   (640, 768, 256), (1024, 12288, 4096)])
+                                   (640, 768, 256), (1024, 12288, 4096), (6144, 12288, 512)])
 def test_swiglu(ctx, M, N, K):
     X = bf(rand(M, K, seed=8))
     Wg = bf(rand(N, K, scale=K ** -0.5, seed=9))
