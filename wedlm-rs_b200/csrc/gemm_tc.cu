@@ -670,8 +670,17 @@ GemmPlan plan_gemm_tc(int M, int N, int K, bool dual, int num_sms) {
   // as the larger units double the split-K partials their consumers read).  Dual
   // (gate/up) already shares the activations between two matrices, and above 128 token
   // rows the accumulators of two tiles would not double-buffer in TMEM.
-  int nb = (!dual && (g.tok_tile <= 128 || wide) && g.n_tiles >= 2) ? 2 : 1;
-  if (const char* e = getenv("WEDLM_GEMM_NB")) nb = atoi(e) == 1 ? 1 : nb;
+  // Below 48 MB of weights (the 4096 x 4096 O projection) the second tile does not pay
+  // for the doubled partials of the few-row case.
+  long big_mb = 48;
+  if (const char* e = getenv("WEDLM_GEMM_NB_MB")) big_mb = atol(e);
+  const bool big = (long)N * K * 2 >= big_mb * 1024 * 1024;
+  int nb = (!dual && ((g.tok_tile <= 128 && big) || wide) && g.n_tiles >= 2) ? 2 : 1;
+  if (const char* e = getenv("WEDLM_GEMM_NB")) {
+    const int f = atoi(e);
+    if (f == 1) nb = 1;
+    if (f == 2 && !dual && g.tok_tile <= 128 && g.n_tiles >= 2) nb = 2;
+  }
   g.nb = nb;
   const int na = dual ? 2 : 1;
   // k-blocks per pipeline stage: larger bulk copies per stage stream faster; keep >= 2
