@@ -15,7 +15,8 @@
 // Both accumulators have TMEM lane = query row, so the thread that owns a query row does
 // its online softmax, rescales its O row when the running max grows, and writes it out.
 // Warp roles: warp 0 TMA producer (Q once, K/V chunks through a 2-stage ring), warp 1
-// TMEM allocator + MMA issuer, warps 2..5 softmax / correction / epilogue.
+// TMEM allocator + MMA issuer, warps 2..9 softmax / correction / epilogue, two threads
+// per query row (64 key columns and 64 O columns each).
 // A work item covering only part of the keys writes (m, l, O) partials; a combine
 // kernel merges them (flash-decoding split-KV).
 #include <cudaTypedefs.h>
@@ -36,7 +37,8 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kThreadsAT = 192;
+constexpr int kThreadsAT = 320;   // warp 0 TMA, warp 1 MMA, warps 2..9 softmax
+constexpr int kSoftThreads = 256;
 constexpr int kQT = 128;        // query rows per tile
 constexpr int kKC = 128;        // keys per chunk (two 64-key pages)
 constexpr int kD = 128;         // head dim (this kernel)
@@ -113,6 +115,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 1);
   int* s_rank = reinterpret_cast<int*>(tmem_slot + 4);  // window ranks of sequence b
   int* s_krank = s_rank + 4096;                          // key ranks of the current chunk
+  float* s_red = reinterpret_cast<float*>(s_krank + kKC);  // [4][128]: row max / sum halves
 
   const AttnWork w = p.work[blockIdx.x];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -224,10 +227,15 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
       tc_commit(kv_empty + ((nchunks > 0 ? nchunks - 1 : 0) % kStages));
     }
   } else {
-    // ---------------- softmax / correction / epilogue (warps 2..5) ----------------
+    // ---------------- softmax / correction / epilogue (warps 2..9) ----------------
+    // Two threads per query row: warp w reads TMEM lanes (w % 4) * 32 .. + 31 and, with
+    // half = (w - 2) / 4, the key / O columns half * 64 .. + 63 of those rows.  The two
+    // halves of a row exchange their maxima and sums through shared memory (s_red).
     const int q4 = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int qr = q4 * 32 + lane;                 // query row within the tile (TMEM lane)
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const uint32_t col0 = (uint32_t)(half * 64);
     const int qi = w.t * kQT + qr;                 // query index within (b, g)
     const bool qvalid = qi < S * p.group;
     const int r_local = qvalid ? qi / p.group : 0;
@@ -238,28 +246,28 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
       ok = mbar_wait(s_full, (uint32_t)i & 1u, p.err, kErrAtSoftS);
       tc_fence_after();
       const int kbase = (w.c0 + i) * kKC;
-      // the chunk's 128 scores of this query row, in registers after one TMEM wait;
-      // masked keys become -inf (log2 units after the scale)
-      float sv[kKC];
-      tmem_ld128(tS + lane_off, sv);
+      // this half's 64 scores of the query row, after one TMEM wait; masked keys become
+      // -inf (log2 units after the scale)
+      float sv[64];
+      tmem_ld64(tS + lane_off + col0, sv);
       float cm = -INFINITY;
       if (kbase + kKC <= L) {  // chunk inside the committed prefix: every key visible
 #pragma unroll
-        for (int j = 0; j < kKC; ++j) {
+        for (int j = 0; j < 64; ++j) {
           sv[j] *= p.scale_log2;
           cm = fmaxf(cm, sv[j]);
         }
       } else {
-        // the chunk's key ranks, one key per softmax thread: cached keys rank below every
-        // query, keys past the window above; then key j is visible iff its rank <= mine
-        {
+        // the chunk's key ranks, one key per first-half thread: cached keys rank below
+        // every query, keys past the window above; key j is visible iff its rank <= mine
+        if (half == 0) {
           const int t = qr - (L - kbase);  // window index of key qr of this chunk
           s_krank[qr] = t < 0 ? INT_MIN : (t < S ? s_rank[t] : INT_MAX);
         }
-        named_bar_sync(1, 128);
-        const int4* kr4 = reinterpret_cast<const int4*>(s_krank);
+        named_bar_sync(1, kSoftThreads);
+        const int4* kr4 = reinterpret_cast<const int4*>(s_krank + half * 64);
 #pragma unroll
-        for (int j4 = 0; j4 < kKC / 4; ++j4) {
+        for (int j4 = 0; j4 < 16; ++j4) {
           const int4 rk = kr4[j4];
           const int r4[4] = {rk.x, rk.y, rk.z, rk.w};
 #pragma unroll
@@ -270,15 +278,20 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
           }
         }
       }
+      // the row's maximum over both halves
+      s_red[half * kQT + qr] = cm;
+      named_bar_sync(1, kSoftThreads);
+      cm = fmaxf(s_red[qr], s_red[kQT + qr]);
       const float mn = fmaxf(m, cm);
       const float base = mn == -INFINITY ? 0.f : mn;
       float ps = 0.f;
       // PV(i-1) must be complete before P is overwritten and O is rescaled
       if (i > 0) ok = ok && mbar_wait(o_done, (uint32_t)(i - 1) & 1u, p.err, kErrAtSoftO);
       tc_fence_after();
-      // P = 2^(s - max) as bf16 into the swizzled K-major P tile (2^-inf = 0 for masked keys)
+      // P = 2^(s - max) as bf16 into K-block `half` of the swizzled K-major P tile
+      // (2^-inf = 0 for masked keys)
 #pragma unroll
-      for (int c = 0; c < kKC / 8; ++c) {
+      for (int c = 0; c < 8; ++c) {
         uint32_t pk[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -287,30 +300,33 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
           ps += __low2float(h2) + __high2float(h2);
           pk[j] = *reinterpret_cast<const uint32_t*>(&h2);
         }
-        const int key0 = c * 8;
-        *reinterpret_cast<uint4*>(sP + (key0 >> 6) * kBlk + sw128_off(qr, key0 & 63)) =
+        *reinterpret_cast<uint4*>(sP + half * kBlk + sw128_off(qr, c * 8)) =
             make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
-      // Rescale this row of O when its running max grew.  tcgen05.ld / st are warp-wide
-      // (.sync.aligned), so the whole warp takes the branch when any of its rows needs it;
-      // rows that do not keep the factor 1.
+      // the row's sum over both halves (first half + second half)
+      s_red[(2 + half) * kQT + qr] = ps;
+      named_bar_sync(1, kSoftThreads);
+      ps = s_red[2 * kQT + qr] + s_red[3 * kQT + qr];
+      // Rescale this half of the O row when its running max grew.  tcgen05.ld / st are
+      // warp-wide (.sync.aligned), so the whole warp takes the branch when any of its rows
+      // needs it; rows that do not keep the factor 1.
       const bool grow = i > 0 && mn > m && m != -INFINITY;
       if (__any_sync(0xffffffffu, grow)) {
         const float f = grow ? fast_exp2(m - mn) : 1.f;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
+        for (int c = 0; c < 4; ++c) {
           float v[16];
-          tmem_ld16(tO + lane_off + c * 16, v);
+          tmem_ld16(tO + lane_off + col0 + c * 16, v);
 #pragma unroll
           for (int j = 0; j < 16; ++j) v[j] *= f;
-          tmem_st16(tO + lane_off + c * 16, v);
+          tmem_st16(tO + lane_off + col0 + c * 16, v);
         }
       }
       l = (m == -INFINITY ? 0.f : l * fast_exp2(m - base)) + ps;
       m = mn;
       fence_proxy_async_smem();
       tc_fence_before();
-      ok = named_bar_and(1, 128, ok);  // the four warps leave the loop together
+      ok = named_bar_and(1, kSoftThreads, ok);  // the eight warps leave the loop together
       if (warp == 2 && lane == 0) mbar_arrive(p_full);
     }
     ok = ok && mbar_wait(o_done, (uint32_t)(nchunks > 0 ? nchunks - 1 : 0) & 1u, p.err,
@@ -319,13 +335,13 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
     const int r = row0 + r_local;
     const int h = g * p.group + (qi % p.group);
     const float inv = l > 0.f ? 1.f / l : 0.f;
-    float ov[kD];
-    tmem_ld128(tO + lane_off, ov);
+    float ov[64];
+    tmem_ld64(tO + lane_off + col0, ov);
     if (ok && qvalid) {
       if (w.part < 0) {
-        __nv_bfloat16* dst = p.out + (long)r * p.ld_out + (long)h * kD;
+        __nv_bfloat16* dst = p.out + (long)r * p.ld_out + (long)h * kD + half * 64;
 #pragma unroll
-        for (int c = 0; c < kD / 8; ++c) {
+        for (int c = 0; c < 8; ++c) {
           uint32_t pk[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -336,14 +352,14 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
           *reinterpret_cast<uint4*>(dst + c * 8) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
       } else {
-        float* po = p.part_o + ((long)w.part * kQT + qr) * kD;
+        float* po = p.part_o + ((long)w.part * kQT + qr) * kD + half * 64;
 #pragma unroll
-        for (int c = 0; c < kD / 4; ++c)
+        for (int c = 0; c < 16; ++c)
           *reinterpret_cast<float4*>(po + 4 * c) =
               make_float4(ov[4 * c], ov[4 * c + 1], ov[4 * c + 2], ov[4 * c + 3]);
       }
     }
-    if (ok && qvalid && w.part >= 0) {
+    if (ok && qvalid && w.part >= 0 && half == 0) {
       p.part_ml[((long)w.part * kQT + qr) * 2] = m;
       p.part_ml[((long)w.part * kQT + qr) * 2 + 1] = l;
     }
@@ -535,7 +551,7 @@ Status run_attention_tc(const AttnArgs& a, const AttnPlan& plan, int* err, cudaS
   p.part_ml = plan.part_ml;
   p.scale_log2 = kLog2e / sqrtf((float)kD);
   p.err = err;
-  const size_t smem = 1024 + (2 + kStages * 4 + 2) * kBlk + 16 * 8 + 4096 * 4 + kKC * 4;
+  const size_t smem = 1024 + (2 + kStages * 4 + 2) * kBlk + 16 * 8 + 4096 * 4 + kKC * 4 + 4 * kQT * 4;
   int dev = 0;
   WEDLM_CUDA_TRY(cudaGetDevice(&dev));
   static unsigned attr_set = 0;

@@ -239,6 +239,18 @@ __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[3
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+// 64 consecutive columns of this warp's 32 TMEM lanes (one wait for the two loads).
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
+  uint32_t r0[32], r1[32];
+  tmem_ld32_nowait(taddr, r0);
+  tmem_ld32_nowait(taddr + 32, r1);
+  tmem_wait_ld();
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    v[i] = __uint_as_float(r0[i]);
+    v[32 + i] = __uint_as_float(r1[i]);
+  }
+}
 // 128 consecutive columns of this warp's 32 TMEM lanes (one wait for the four loads).
 __device__ __forceinline__ void tmem_ld128(uint32_t taddr, float (&v)[128]) {
   uint32_t r0[32], r1[32], r2[32], r3[32];
