@@ -811,14 +811,24 @@ def bench_decode_8b(args, rank, ws, local):
         return {"metric": METRIC, "value": round(value, 2), "unit": "committed tok/s",
                 "ms_per_step": round(ms_max, 3), "kernel_classes": prof,
                 "note": "profiling run (no e2e)"}
-    # end to end through the public generate call: prompt from host, ids back to host
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier(ws)
-    e0.record(stream)
-    ids, est = ctx.generate_streaming(prompt, NEW_8B, WINDOW_8B, params)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_s = max_over_ranks(e0.elapsed_time(e1) / 1e3, ws)
+    # end to end through the public generate call: prompt from host, ids back to host.
+    # Three calls; the median is reported (one call spans 513 host round trips, and a
+    # host-side stall on a shared machine lands in one call, not in all three).
+    runs = []
+    eclk = ClockSampler(local)
+    eclk.start()
+    time.sleep(0.3)
+    et0 = time.time()
+    for _ in range(3):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(ws)
+        e0.record(stream)
+        ids, est = ctx.generate_streaming(prompt, NEW_8B, WINDOW_8B, params)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        runs.append(max_over_ranks(e0.elapsed_time(e1) / 1e3, ws))
+    e2e_clocks = eclk.stop(et0, time.time())
+    e2e_s = sorted(runs)[1]
     e2e_tok = float(est["tokens_generated"])
     e2e_steps = float(est["steps"])
     if ws > 1:
@@ -874,6 +884,8 @@ def bench_decode_8b(args, rank, ws, local):
                 "h2d_bytes_per_step": int((h1 - h0) / steps_timed),
                 "d2h_bytes_per_step": int((d1 - d0) / steps_timed),
                 "tokens": int(e2e_tok), "steps_per_sequence": round(e2e_steps, 1),
+                "runs_s": [round(r, 4) for r in runs], "of_runs": "median of 3 calls",
+                "clocks": e2e_clocks,
                 "scope": "wedlm_generate_streaming: 512-token prompt prefill + up to 512 "
                          "tokens (fewer when EOS is generated), host ids in and out"},
         "gpu_launches": int(launches),
