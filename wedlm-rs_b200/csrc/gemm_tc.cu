@@ -65,7 +65,7 @@ struct TcParams {
   int packed;
   float* slots;        // slot mode: [tiles][maxc][na][tok_tile][128]
   int slot_mode, maxc;
-  int poll, nohint;   // tuning: spin on test_wait; plain bulk copies without L2 hint
+  int poll, nohint;   // tuning: spin on test_wait; weight copies evict-last, not evict-first
   int vec_ok;          // out / resid rows 16-byte aligned
 };
 
