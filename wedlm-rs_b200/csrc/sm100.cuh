@@ -251,22 +251,6 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
     v[32 + i] = __uint_as_float(r1[i]);
   }
 }
-// 128 consecutive columns of this warp's 32 TMEM lanes (one wait for the four loads).
-__device__ __forceinline__ void tmem_ld128(uint32_t taddr, float (&v)[128]) {
-  uint32_t r0[32], r1[32], r2[32], r3[32];
-  tmem_ld32_nowait(taddr, r0);
-  tmem_ld32_nowait(taddr + 32, r1);
-  tmem_ld32_nowait(taddr + 64, r2);
-  tmem_ld32_nowait(taddr + 96, r3);
-  tmem_wait_ld();
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    v[i] = __uint_as_float(r0[i]);
-    v[32 + i] = __uint_as_float(r1[i]);
-    v[64 + i] = __uint_as_float(r2[i]);
-    v[96 + i] = __uint_as_float(r3[i]);
-  }
-}
 
 // Shared-memory matrix descriptor: K-major tile whose rows are 128 bytes, stored with
 // the 128-byte swizzle; 8-row core groups are 1024 bytes apart (tile base 1024-aligned).
