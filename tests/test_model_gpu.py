@@ -396,3 +396,56 @@ def test_vocab_sharded_lm_head_and_entropy():
     n = int(ref["n_selected"][0])
     assert int(got["n_selected"][0]) == n
     assert torch.equal(got["selected"][:n], ref["selected"][:n])
+
+
+@pytest.mark.parametrize("mode", ["streaming", "block", "autoregressive"])
+def test_c1_eos_stops_like_oracle(mode):
+    """EOS inside a commit (wedlm.rs:475-488), inside a filled block and in the
+    autoregressive loop (engine.rs:160-217): the end-of-sequence id is set to a token the
+    decode produces early (found with the oracle under an id it never emits), and the
+    CUDA path stops where the oracle does."""
+    import dataclasses
+    from wedlm_b200 import Context
+    base = c1_config()
+    w = random_weights(base, seed=0, std=0.02)
+    prompt = np.random.default_rng(31).integers(1, 4095, size=24).tolist()
+    p = params(9.0, 0.01, 3)
+    osp = OSP(temperature=0.0, entropy_threshold=9.0, distance_penalty=0.01,
+              max_tokens_per_step=3)
+    free = dataclasses.replace(base, eos_token_id=4094)
+    om = OracleModel(free, w, "f32")
+    if mode == "streaming":
+        ref0, _ = OracleDecoder(om, free.mask_token_id, 4094).generate_streaming(prompt, 24, 12, osp)
+        out0 = ref0[len(prompt):]
+    elif mode == "block":
+        _, out0, _ = OracleDecoder(om, free.mask_token_id, 4094).generate_block(prompt, 16, osp)
+    else:
+        out0, seq = [], list(prompt)
+        for _ in range(8):
+            lg, _ = om.forward(seq)
+            t = int(len(lg[-1]) - 1 - np.argmax(np.asarray(lg[-1])[::-1]))
+            out0.append(t)
+            seq.append(t)
+    eos = int([t for t in out0 if t != free.mask_token_id][3])
+    cfg = dataclasses.replace(base, eos_token_id=eos)
+    om = OracleModel(cfg, w, "f32")
+    dec = OracleDecoder(om, cfg.mask_token_id, cfg.eos_token_id)
+    ctx = Context(to_model_config(cfg, max_block_tokens=32), max_seqs=1, max_ctx=256)
+    try:
+        ctx.load_weights(w)
+        if mode == "streaming":
+            ids, st = ctx.generate_streaming(prompt, 24, 12, p)
+            ref, rst = dec.generate_streaming(prompt, 24, 12, osp)
+            assert ids == ref and ids[-1] == eos and len(ids) < len(prompt) + 24
+            assert st["tokens_generated"] == rst.tokens_generated
+        elif mode == "block":
+            ctx.reset_sequence(0)
+            ids, blk, st = ctx.generate_block(prompt, 16, p)
+            rids, rblk, rst = dec.generate_block(prompt, 16, osp)
+            assert blk == rblk and eos in blk and st["steps"] == rst.steps
+        else:
+            ids = ctx.generate_autoregressive(prompt, 8)
+            assert ids[-1] == eos and len(ids) < 8 and ids == out0[:len(ids)]
+        ctx.check_device_error()
+    finally:
+        ctx.close()
