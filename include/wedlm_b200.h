@@ -185,12 +185,15 @@ WEDLM_API int wedlm_entropy_select(wedlm_ctx* ctx, const void* logits, int dtype
  * wedlm_entropy_select; the kernels' scratch lives in a fixed 167,936-byte static
  * device array instead of context buffers that grow by cudaMalloc after a device-wide
  * synchronisation.  Limits per call: rows <= 4096, nseq <= 1024 and rows x vocabulary
- * splits <= 8192 (splits = ceil(4 * SMs / rows) capped at ceil(V / 8192)); larger
- * calls fail with WEDLM_ERR_INVALID_ARG and launch nothing.  The scratch address is
- * looked up per device on the first call, so make one call on each device before
- * any stream capture.  The scratch is shared by every caller in the process on that
- * device: calls that overlap in time (two streams, or two threads) race on it and
- * must be serialised by the caller. */
+ * splits <= 8192 (splits = ceil(4 * SMs / rows) capped at ceil(V / 8192), so on a
+ * 148-SM B200 rows x splits < rows + 592 and only the first two limits can bind);
+ * larger calls fail with WEDLM_ERR_INVALID_ARG and launch nothing.  rows = 0 zeroes
+ * n_selected.  The scratch address is looked up per device on the first call and
+ * kept for the life of the process, so make one call on each device before any
+ * stream capture, and do not reset the device (cudaDeviceReset) between calls.  The
+ * scratch is shared by every caller in the process on that device: calls that overlap
+ * in time (two streams, or two threads) race on it and must be serialised by the
+ * caller. */
 WEDLM_API int wedlm_entropy_select_noalloc(wedlm_ctx* ctx, const void* logits, int dtype,
                                            int rows, int V, int ld, float temperature,
                                            float tau, float lambda, int nseq,

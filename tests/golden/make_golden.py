@@ -13,13 +13,15 @@
    the oracle: per-step reordered ids/positions, entropies, selections, committed
    ids.  It is a regression record for the CUDA path, produced by the oracle.
 
-Usage: ``python tests/golden/make_golden.py [--reference /path/to/WeDLM-rs]``.
+Usage: ``python tests/golden/make_golden.py [--reference /path/to/WeDLM-rs]`` (or set
+``WEDLM_REFERENCE``).
 Needs the reference checkout only for (1).
 """
 from __future__ import annotations
 
 import argparse
 import json
+import os
 import subprocess
 import sys
 import tempfile
@@ -93,10 +95,11 @@ def make_c1() -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("WEDLM_REFERENCE"),
+                    help="WeDLM-rs checkout (default: $WEDLM_REFERENCE)")
     a = ap.parse_args()
-    ref = Path(a.reference)
-    if (ref / "scripts" / "generate_parity_fixture.py").exists():
+    ref = Path(a.reference) if a.reference else None
+    if ref is not None and (ref / "scripts" / "generate_parity_fixture.py").exists():
         make_ref_fixture(ref)
     else:
         print("reference checkout not found; keeping the committed ref_parity_small.json")

@@ -120,6 +120,19 @@ def test_multiple_sequences_and_empty(ctx):
     assert out["n_selected"][1] == 0 and out["n_selected"][5] == 0
 
 
+def test_empty_row_set(ctx):
+    """No rows: the selection counts are zeroed and the partials entry point is a no-op
+    (the split plan must not divide by the row count)."""
+    t = torch.empty(0, 151936, dtype=torch.bfloat16, device="cuda")
+    sr = torch.tensor([0, 0, 0], dtype=torch.int32, device="cuda")
+    mp = torch.empty(0, dtype=torch.int32, device="cuda")
+    cp = torch.tensor([8, 8], dtype=torch.int32, device="cuda")
+    out = ctx.entropy_select(t, 0.0, 0.8, 0.05, sr, mp, cp)
+    parts = ctx.entropy_partials(t, 0, 0.0)
+    torch.cuda.synchronize()
+    assert out["n_selected"].tolist() == [0, 0] and parts.shape == (0, 4)
+
+
 def test_ties_resolve_to_last_index(ctx):
     V = 5000
     x = np.zeros((3, V), np.float32)

@@ -85,6 +85,21 @@ def test_no_device_memory_taken_per_call(ctx):
     compare(outs[2], outs[0], sr)
 
 
+def test_empty_row_set(ctx):
+    """No mask rows at all: both entry points report zero selections per sequence (the
+    plan must not divide by the row count) and the static scratch stays usable."""
+    logits, sr, mp, cp = case([0, 0], 151936, torch.bfloat16, 5)
+    got = outputs(0, 2)
+    got["n_selected"].fill_(7)
+    ctx.entropy_select_noalloc(logits, 0.0, 0.8, 0.05, sr, mp, cp, got)
+    want = ctx.entropy_select(logits, 0.0, 0.8, 0.05, sr, mp, cp)
+    torch.cuda.synchronize()
+    assert got["n_selected"].tolist() == [0, 0] and want["n_selected"].tolist() == [0, 0]
+    logits, sr, mp, cp = case([40, 56], 151936, torch.bfloat16, 6)
+    after = ctx.entropy_select_noalloc(logits, 0.0, 0.8, 0.05, sr, mp, cp, outputs(96, 2))
+    compare(after, ctx.entropy_select(logits, 0.0, 0.8, 0.05, sr, mp, cp), sr)
+
+
 @pytest.mark.parametrize("rows_per_seq,V", [
     ([4097], 16),          # rows above 4096
     ([1] * 1025, 16),      # nseq above 1024

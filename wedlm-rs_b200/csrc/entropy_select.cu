@@ -510,6 +510,8 @@ entropy_combine_kernel(const float* __restrict__ part, int nshards, long shard_s
 }
 
 int pick_splits(int rows, int V, int num_sms) {
+  // No rows: no launch follows; one split keeps the plan's arithmetic defined.
+  if (rows <= 0 || V <= 0) return 1;
   // Aim for >= 4 CTAs per SM in total, with >= 8K columns per CTA.
   int target = num_sms * 4;
   int splits = (target + rows - 1) / rows;
@@ -561,7 +563,7 @@ EntropyPlan plan_entropy(int rows, int V, int dtype, int num_sms) {
 }
 
 Status check_entropy_args(const EntropyArgs& A) {
-  WEDLM_CHECK_ARG(A.logits != nullptr, "logits is NULL");
+  WEDLM_CHECK_ARG(A.logits != nullptr || A.rows == 0, "logits is NULL");
   WEDLM_CHECK_ARG(A.dtype == WEDLM_F32 || A.dtype == WEDLM_BF16, "logits dtype must be F32 or BF16");
   WEDLM_CHECK_ARG(A.rows >= 0 && A.V > 0 && A.ld >= A.V, "bad rows / V / ld");
   return Status::ok();
@@ -571,12 +573,14 @@ Status run_entropy_select(const EntropyArgs& A, const EntropyScratch& W, int num
                           cudaStream_t st) {
   WEDLM_TRY(check_entropy_args(A));
   WEDLM_CHECK_ARG(A.nseq >= 1, "nseq must be >= 1");
-  WEDLM_CHECK_ARG(A.seq_rows && A.mask_pos && A.caps && A.selected && A.n_selected,
-                  "seq_rows, mask_pos, caps, selected and n_selected are required");
+  WEDLM_CHECK_ARG(A.n_selected != nullptr, "n_selected is required");
   if (A.rows == 0) {
+    // no mask rows: every sequence selects nothing (the per-row outputs are empty)
     WEDLM_CUDA_TRY(cudaMemsetAsync(A.n_selected, 0, sizeof(int) * A.nseq, st));
     return Status::ok();
   }
+  WEDLM_CHECK_ARG(A.seq_rows && A.mask_pos && A.caps && A.selected,
+                  "seq_rows, mask_pos, caps, selected and n_selected are required");
   EntropyPlan p = plan_entropy(A.rows, A.V, A.dtype, num_sms);
   WEDLM_CHECK_ARG((long)A.rows * p.splits * 4 <= W.partial_capacity, "entropy scratch too small");
   WEDLM_CHECK_ARG(A.rows <= W.row_capacity && A.nseq <= W.seq_capacity, "entropy scratch too small");
@@ -592,8 +596,8 @@ Status run_entropy_select(const EntropyArgs& A, const EntropyScratch& W, int num
 Status run_entropy_partials(const EntropyArgs& A, const EntropyScratch& W, int vocab_offset,
                             float* out, int num_sms, cudaStream_t st) {
   WEDLM_TRY(check_entropy_args(A));
+  if (A.rows == 0) return Status::ok();  // nothing to reduce (the buffers may be empty)
   WEDLM_CHECK_ARG(out != nullptr, "partials output is NULL");
-  if (A.rows == 0) return Status::ok();
   EntropyPlan p = plan_entropy(A.rows, A.V, A.dtype, num_sms);
   WEDLM_CHECK_ARG((long)A.rows * p.splits * 4 <= W.partial_capacity, "entropy scratch too small");
   WEDLM_CHECK_ARG(A.rows <= W.row_capacity, "entropy scratch too small");

@@ -323,14 +323,23 @@ extern "C" int wedlm_load_weights(wedlm_ctx* ctx, const char* model_dir) {
       std::vector<int64_t> shape;
       uint64_t numel = 1;
       for (const Json& d : sh->arr) {
-        if (d.kind != Json::kNum || d.num < 0)
+        // dimensions are whole numbers below 2^62; their product must not wrap
+        if (d.kind != Json::kNum || d.num < 0 || d.num >= 4.6e18 || d.num != (double)(uint64_t)d.num)
           return ctx->fail(Status::err(WEDLM_ERR_IO, path + ": bad shape of " + name));
         shape.push_back((int64_t)d.num);
-        numel *= (uint64_t)d.num;
+        if (__builtin_mul_overflow(numel, (uint64_t)d.num, &numel))
+          return ctx->fail(Status::err(WEDLM_ERR_IO, path + ": shape of " + name + " overflows"));
       }
+      uint64_t nbytes = 0;
+      if (__builtin_mul_overflow(numel, (uint64_t)esz, &nbytes))
+        return ctx->fail(Status::err(WEDLM_ERR_IO, path + ": shape of " + name + " overflows"));
+      // both offsets must be numbers before either value is read
+      if (off->arr[0].kind != Json::kNum || off->arr[1].kind != Json::kNum ||
+          off->arr[0].num < 0 || off->arr[1].num < 0 || off->arr[0].num >= 1.8e19 ||
+          off->arr[1].num >= 1.8e19)
+        return ctx->fail(Status::err(WEDLM_ERR_IO, path + ": bad data_offsets of " + name));
       const uint64_t b = (uint64_t)off->arr[0].num, e = (uint64_t)off->arr[1].num;
-      if (off->arr[0].kind != Json::kNum || off->arr[1].kind != Json::kNum || b > e ||
-          e > data_size || e - b != numel * (uint64_t)esz)
+      if (b > e || e > data_size || e - b != nbytes)
         return ctx->fail(Status::err(WEDLM_ERR_IO, path + ": bad data_offsets of " + name));
       if (shape.empty() || shape.size() > 2)
         return ctx->fail(Status::err(WEDLM_ERR_INVALID_ARG, name + ": expected 1 or 2 dimensions"));
