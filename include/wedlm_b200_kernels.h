@@ -75,6 +75,16 @@ WEDLM_API int wedlm_kernel_sample(wedlm_ctx* ctx, const void* logits, int dtype,
  * inside a kernel since the last check: WEDLM_ERR_TIMEOUT, else WEDLM_OK. */
 WEDLM_API int wedlm_check_device_error(wedlm_ctx* ctx, void* stream);
 
+/* Test of the bounded device wait (no counterpart in the reference, whose host code
+ * has no device waits): launches one CTA whose consumer warp waits, with the helper the
+ * tcgen05 kernels use, on an mbarrier phase that nothing completes (no arrival, no copy
+ * in flight).  After limit_ns (0 < limit_ns <= 2e9) the wait gives up, records wait site
+ * 1 in the context's error word and the kernel returns; wedlm_check_device_error then
+ * reports WEDLM_ERR_TIMEOUT.  out: device int32[2] = {wait succeeded (0 expected),
+ * microseconds waited}. */
+WEDLM_API int wedlm_kernel_wait_probe(wedlm_ctx* ctx, int64_t limit_ns, int32_t* out,
+                                      void* stream);
+
 /* Kernel classes of the profiler. */
 enum wedlm_kernel_class {
   WEDLM_KC_GEMM = 0,       /* projection GEMMs (tcgen05) incl. their shared-tile reduce */

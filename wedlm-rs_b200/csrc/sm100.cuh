@@ -97,16 +97,22 @@ __device__ __forceinline__ bool mbar_spin(uint64_t* bar, uint32_t parity, int* e
   if (err) atomicCAS(err, 0, code);
   return false;
 }
-// Bounded wait for the phase with the given parity to complete.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+// Bounded wait for the phase with the given parity to complete: gives up after
+// `limit_ns` nanoseconds or kWaitLimit polls, records `code` in *err (first failure
+// wins) and returns false.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, int* err, int code,
+                                              uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   for (uint32_t i = 0; i < kWaitLimit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63u) == 63u && global_ns() - t0 > kWaitNs) break;
+    if ((i & 63u) == 63u && global_ns() - t0 > limit_ns) break;
   }
   if (err) atomicCAS(err, 0, code);
   return false;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  return mbar_wait_for(bar, parity, err, code, kWaitNs);
 }
 
 // ---- TMA -------------------------------------------------------------------------

@@ -98,6 +98,7 @@ _PROTOS = {
                                     C.c_int, C.c_int, C.c_int, P, C.c_int64, P, C.c_int64, P]),
     "wedlm_kernel_pack_weight": (C.c_int, [P, P, C.c_int64, C.c_int, C.c_int, P, P]),
     "wedlm_check_device_error": (C.c_int, [P, P]),
+    "wedlm_kernel_wait_probe": (C.c_int, [P, C.c_int64, P, P]),
     "wedlm_load_weights": (C.c_int, [P, C.c_char_p]),
     "wedlm_generate_block": (C.c_int, [P, C.c_int, P, C.c_int, C.c_int,
                                        C.POINTER(WedlmSamplingParams), P,

@@ -264,6 +264,15 @@ class Context:
     def check_device_error(self, stream=None):
         check(lib().wedlm_check_device_error(self.h, stream_ptr(stream)), self.h)
 
+    def wait_probe(self, limit_ns: int, stream=None):
+        """Launch the bounded-wait probe (a wait that nothing completes); returns the
+        device int32 tensor {wait succeeded, microseconds waited}."""
+        import torch
+        out = torch.full((2,), -1, dtype=torch.int32, device=f"cuda:{self.device}")
+        check(lib().wedlm_kernel_wait_probe(self.h, int(limit_ns), ptr(out), stream_ptr(stream)),
+              self.h)
+        return out
+
     # ---- model: weights ---------------------------------------------------------------
     def load_safetensors(self, model_dir: str) -> None:
         """All model tensors from ``model_dir`` (model.safetensors, or the shards of
