@@ -189,12 +189,48 @@ def softmax(x: np.ndarray, axis: int = -1) -> np.ndarray:
     return (e / np.sum(e, axis=axis, keepdims=True, dtype=np.float32)).astype(np.float32)
 
 
+class _WeightStore:
+    """Weights by name.  f32 arrays are rounded once at construction (bf16 mode);
+    uint16 arrays are bf16 bit patterns kept as they are and widened to f32 on each
+    access (exact: every bf16 value is an f32 value), so that a model with billions of
+    parameters is held at two bytes per weight."""
+
+    def __init__(self, weights: Dict[str, np.ndarray], rnd):
+        self._a = {}
+        for k, v in weights.items():
+            v = np.asarray(v)
+            self._a[k] = v if v.dtype == np.uint16 else rnd(v)
+
+    def __getitem__(self, name: str) -> np.ndarray:
+        v = self._a[name]
+        return bf16_bits_to_f32(v) if v.dtype == np.uint16 else v
+
+    def rows(self, name: str, idx) -> np.ndarray:
+        """Rows ``idx`` of a matrix, widened after the gather."""
+        v = self._a[name][np.asarray(idx)]
+        return bf16_bits_to_f32(v) if v.dtype == np.uint16 else v
+
+    def row_block(self, name: str, r0: int, r1: int) -> np.ndarray:
+        v = self._a[name][r0:r1]
+        return bf16_bits_to_f32(v) if v.dtype == np.uint16 else v
+
+    def shape(self, name: str):
+        return self._a[name].shape
+
+    def keys(self):
+        return self._a.keys()
+
+
 class OracleModel:
     """``WeDLMForCausalLM`` restated in numpy.
 
     ``cache`` is a list (one per layer) of ``(K, V)`` with shape ``[n_kv, L, d]``;
     K is stored post-QK-norm, post-RoPE, V raw (``attention.rs:154-184``).
+    ``weights`` values are f32 arrays, or uint16 arrays of bf16 bit patterns (held as
+    such; see ``_WeightStore``).
     """
+
+    LM_HEAD_CHUNK = 16384  # vocabulary rows per LM-head product (bounds the f32 copy)
 
     def __init__(self, cfg: WeDLMConfig, weights: Dict[str, np.ndarray], dtype: str = "f32"):
         assert dtype in ("f32", "bf16")
@@ -202,9 +238,19 @@ class OracleModel:
         self.dtype = dtype
         rnd = bf16_round if dtype == "bf16" else (lambda a: np.asarray(a, np.float32))
         self._r = rnd
-        self.w = {k: rnd(v) for k, v in weights.items()}
+        self.w = _WeightStore(weights, rnd)
         self.cos, self.sin = rope_tables(cfg.head_dim, cfg.max_position_embeddings,
                                          cfg.rope_theta, dtype == "bf16")
+
+    def _lm_head(self, h: np.ndarray) -> np.ndarray:
+        """``h @ lm_head.T`` (``causal_lm.rs:77``) in vocabulary chunks, f32 accumulate."""
+        V = self.w.shape("lm_head.weight")[0]
+        out = np.empty((h.shape[0], V), np.float32)
+        for v0 in range(0, V, self.LM_HEAD_CHUNK):
+            v1 = min(V, v0 + self.LM_HEAD_CHUNK)
+            out[:, v0:v1] = np.matmul(h, self.w.row_block("lm_head.weight", v0, v1).T,
+                                      dtype=np.float32)
+        return out
 
     # -- helpers ---------------------------------------------------------------
     def _lin(self, x, name):
@@ -268,7 +314,7 @@ class OracleModel:
             raise ValueError("position out of range of the RoPE table")
         S = ids.shape[0]
         rank = np.arange(S) if rank is None else np.asarray(rank).reshape(-1)
-        h = self.w["model.embed_tokens.weight"][ids].astype(np.float32)
+        h = self.w.rows("model.embed_tokens.weight", ids).astype(np.float32)
         new = []
         for l in range(self.cfg.num_hidden_layers):
             c = kv_caches[l] if kv_caches is not None else None
@@ -279,7 +325,7 @@ class OracleModel:
             h = h[logits_rows]
         if return_hidden:
             return h, new
-        logits = np.matmul(h, self.w["lm_head.weight"].T, dtype=np.float32)
+        logits = self._lm_head(h)
         if round_logits:
             logits = self._r(logits)
         return logits, new
@@ -295,7 +341,7 @@ class OracleModel:
         the LM head (what ``cache_prefix`` keeps, ``wedlm.rs:85-96``)."""
         ids = np.asarray(input_ids, dtype=np.int64).reshape(-1)
         pos = np.arange(ids.shape[0])
-        h = self.w["model.embed_tokens.weight"][ids].astype(np.float32)
+        h = self.w.rows("model.embed_tokens.weight", ids).astype(np.float32)
         new = []
         for l in range(self.cfg.num_hidden_layers):
             h, kv = self._layer(l, h, pos, None, np.arange(ids.shape[0]))

@@ -1,0 +1,229 @@
+"""Decode-level parity of the bf16 tensor-core path at the 8B widths, full vocabulary.
+
+Model: hidden 4096, 32/8 heads, head_dim 128, SwiGLU 12288, vocab 151936 (the 8B
+shape with 4 of its 36 layers), bf16 weights N(0, 0.02^2) drawn on the device
+(``wedlm_init_random``) and read back as bf16 bit patterns for the oracle, so both
+sides hold the same weights.  Every forward runs on the production kernels: the
+tcgen05 GEMMs, the tcgen05 block attention, the fused RoPE / QK-norm / KV append and
+the fused entropy-select.
+
+Lockstep: the oracle's streaming decoder (``wedlm.rs:336-590``) drives a model whose
+every forward runs both on the GPU and in the bf16 oracle (``causal_lm.rs:68-79``)
+from the same window and the same committed tokens, and continues with the GPU's
+logits.  At every step:
+
+* logits of the mask rows (LM head written as f32, i.e. before the final bf16
+  rounding) against the bf16 oracle: max |err| <= LOGIT_MAX_ABS, mean <= LOGIT_MEAN.
+  The north-star figure of 2e-2 max-abs is below the rounding noise of bf16 itself at
+  these widths: the bf16 oracle differs from the exact f32 computation by ~0.1 max-abs
+  on the same weights (module constants), so no bf16 implementation that rounds where
+  the reference rounds can be held to 2e-2;
+* entropies of the fused kernel on the GPU's bf16 logits against the oracle's
+  entropies of the oracle's bf16 logits (``sampler.rs:125-154``): within H_TOL = 1e-3;
+* the committed set (``select_by_entropy_with_distance``, ``sampler.rs:446-493``, with
+  the step's EMA cap) equal to the oracle's wherever the decision margin exceeds H_TOL,
+  and each committed token (greedy, last-max argmax, ``sampler.rs:183-190``) equal to
+  the oracle's argmax wherever the oracle's top-2 logit gap exceeds twice the step's
+  largest logit error.
+
+Then the production loops (``wedlm_generate_streaming`` and the step-wise
+``wedlm_decode_begin / step``) run the same decode from the prompt on their own and
+must commit exactly the lockstep trajectory's tokens.  Two parameter sets: tau 0.8
+(random-init entropy ~11.1 nats, so every step takes the fallback branch) and tau
+11.5 (the threshold branch: the rows within ~8 slots of the frontier pass, capped).
+"""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+from oracle.decoder import OracleDecoder
+from oracle.model import OracleModel, bf16_round, weight_names
+from oracle.sampler import SamplingParams as OSP, compute_entropies_with_probs, \
+    select_by_entropy_with_distance
+from model_configs import to_model_config, wide_bf16_config
+
+LAYERS = 4
+VOCAB = 151936
+H_TOL = 1e-3
+# Logit error of the GPU path against the bf16 oracle after 4 layers (mask rows, before
+# the final rounding).  Measured on B200 over the steps below: max 0.099-0.104, mean
+# 0.0147-0.0156; on the same weights the bf16 oracle is itself max 0.105 / mean 0.0158
+# from the exact f32 computation, and the GPU path max 0.115 / mean 0.0163 from it.  The
+# bounds leave ~1.4x headroom over the measured values.
+LOGIT_MAX_ABS = 0.15
+LOGIT_MEAN = 0.022
+PROMPT = 64
+WINDOW = 96
+
+
+@pytest.fixture(scope="module")
+def model8():
+    from wedlm_b200 import Context
+    cfg = wide_bf16_config(layers=LAYERS, vocab=VOCAB)
+    ctx = Context(to_model_config(cfg, max_block_tokens=WINDOW), max_seqs=3, max_ctx=512)
+    ctx.init_random(seed=11, std=0.02)
+    bits = {name: ctx.get_weight(name, shape) for name, shape in weight_names(cfg)}
+    om = OracleModel(cfg, bits, "bf16")
+    yield cfg, ctx, bits, om
+    ctx.close()
+
+
+class Lockstep:
+    """The model the oracle decoder drives: each forward runs on the GPU (through the C
+    ABI) and in the bf16 oracle from the same inputs; the decoder continues with the
+    GPU's logits, so it follows the GPU's trajectory while every step is checked."""
+
+    def __init__(self, ctx, om, mask, seq):
+        self.ctx, self.om, self.mask, self.seq = ctx, om, mask, seq
+        self.steps = []
+
+    def prefill_cache(self, ids):
+        self.ctx.reset_sequence(self.seq)
+        self.ctx.prefill(self.seq, np.asarray(ids))
+        return self.om.prefill_cache(ids)
+
+    def forward_with_positions(self, ids, positions, cache):
+        from wedlm_b200 import Context
+        ids = np.asarray(ids, dtype=np.int64)
+        pos = np.asarray(positions, dtype=np.int64)
+        L = cache[0][0].shape[1]
+        gl = self.ctx.cache_len(self.seq)
+        if gl < L:
+            self.ctx.commit(self.seq, L - gl)  # the decoder kept the committed prefix
+        assert self.ctx.cache_len(self.seq) == L
+        S = len(ids)
+        nf = int((ids != self.mask).sum())
+        nm = S - nf
+        assert (ids[nf:] == self.mask).all()
+        lg = self.ctx.forward_with_positions([self.seq], ids[None], pos[None],
+                                             logit_row_begin=[nf], logits_dtype=torch.float32)
+        ref, new_cache = self.om.forward_with_positions(ids, pos, cache, logits_rows=slice(nf, S),
+                                                        round_logits=False)
+        rec = {"nf": nf, "nm": nm}
+        if nm:
+            g = lg.cpu().numpy()
+            err = np.abs(g - ref)
+            rec["err_max"], rec["err_mean"] = float(err.max()), float(err.mean())
+            # the fused entropy-select kernel on the GPU's bf16 logits (the production input)
+            kc = Context(None)
+            try:
+                o = kc.entropy_select(lg.to(torch.bfloat16).contiguous(), 0.0, 0.8, 0.05,
+                                      torch.tensor([0, nm], dtype=torch.int32, device="cuda"),
+                                      torch.arange(nm, dtype=torch.int32, device="cuda"),
+                                      torch.tensor([1], dtype=torch.int32, device="cuda"))
+                torch.cuda.synchronize()
+                rec["H_kernel"] = o["H"].cpu().numpy()
+                rec["argmax_kernel"] = o["argmax"].cpu().numpy()
+            finally:
+                kc.close()
+            refb = bf16_round(ref)
+            rec["H_oracle"], _ = compute_entropies_with_probs(refb, 0.0)
+            srt = np.sort(refb, axis=-1)
+            rec["gap_oracle"] = srt[:, -1] - srt[:, -2]
+            rec["argmax_oracle"] = (refb.shape[1] - 1 - np.argmax(refb[:, ::-1], axis=-1))
+            out = np.zeros((S, g.shape[1]), np.float32)
+            out[nf:] = bf16_round(g)
+        else:
+            out = np.zeros((S, 1), np.float32)
+        self.steps.append(rec)
+        return out, new_cache
+
+
+@pytest.mark.parametrize("tau,lam,cap,max_new", [(0.8, 0.05, 8, 6), (11.5, 0.05, 8, 24)])
+def test_bf16_8b_widths_decode_lockstep(model8, tau, lam, cap, max_new):
+    from wedlm_b200 import SamplingParams
+    cfg, ctx, bits, om = model8
+    prompt = np.random.default_rng(int(tau * 10)).integers(0, VOCAB - 2, size=PROMPT).tolist()
+    osp = OSP(temperature=0.0, entropy_threshold=tau, distance_penalty=lam,
+              max_tokens_per_step=cap)
+    ls = Lockstep(ctx, om, cfg.mask_token_id, seq=0)
+    dec = OracleDecoder(ls, cfg.mask_token_id, cfg.eos_token_id)
+    ids, st = dec.generate_streaming(prompt, max_new, WINDOW, osp)
+    checked_sel = checked_tok = 0
+    worst = {"err_max": 0.0, "err_mean": 0.0, "dH_kernel_oracle": 0.0}
+    for rec, tr in zip(ls.steps, dec.trace):
+        if rec["nm"] == 0:
+            continue
+        assert rec["err_max"] <= LOGIT_MAX_ABS and rec["err_mean"] <= LOGIT_MEAN, rec
+        worst["err_max"] = max(worst["err_max"], rec["err_max"])
+        worst["err_mean"] = max(worst["err_mean"], rec["err_mean"])
+        # the kernel's entropies vs the oracle's (of the oracle's own logits)
+        dH = np.abs(rec["H_kernel"] - rec["H_oracle"]).max()
+        worst["dH_kernel_oracle"] = max(worst["dH_kernel_oracle"], float(dH))
+        assert dH <= H_TOL, dH
+        # the kernel's entropies vs the reference rule on the same (GPU) logits
+        assert np.abs(rec["H_kernel"] - np.asarray(tr.entropies)).max() <= 1e-4
+        # committed set: the oracle's selection on its own entropies
+        mpos = tr.mask_logical_indices
+        osel = select_by_entropy_with_distance(rec["H_oracle"].tolist(), mpos, tau, lam,
+                                               tr.effective_max)
+        adj = rec["H_oracle"] + np.float32(lam) * (np.asarray(mpos) - min(mpos))
+        srt = np.sort(adj)
+        margin = min(np.abs(adj - tau).min(), (srt[1] - srt[0]) if len(srt) > 1 else 1.0)
+        if margin > H_TOL:
+            assert tr.selected == osel, (tr.selected, osel, margin)
+            checked_sel += 1
+        # committed tokens: GPU argmax (last max) vs the oracle's where the gap allows
+        for s, t in zip(tr.selected, tr.sampled):
+            assert t == rec["argmax_kernel"][s]
+            if rec["gap_oracle"][s] > 2 * rec["err_max"]:
+                assert t == rec["argmax_oracle"][s], (s, t, rec["argmax_oracle"][s])
+                checked_tok += 1
+    assert checked_sel >= 2 and checked_tok >= 2, (checked_sel, checked_tok)
+    print(f"\n[8B-widths bf16 lockstep tau={tau}] steps={st.steps} "
+          f"tokens={st.tokens_generated} logits vs bf16 oracle: max {worst['err_max']:.4f} "
+          f"mean {worst['err_mean']:.5f}; |H kernel - H oracle| max {worst['dH_kernel_oracle']:.2e}; "
+          f"selections checked {checked_sel}, tokens checked {checked_tok}")
+
+    # the production loops, on their own from the prompt, commit the same tokens
+    params = SamplingParams(temperature=0.0, entropy_threshold=tau, distance_penalty=lam,
+                            max_tokens_per_step=cap)
+    out, pst = ctx.generate_streaming(prompt, max_new, WINDOW, params, seq=1)
+    assert out == ids, (out[PROMPT:], ids[PROMPT:])
+    assert pst["steps"] == st.steps and pst["tokens_generated"] == st.tokens_generated
+    ctx.decode_begin([2], [prompt], max_new, WINDOW, params)
+    live = 1
+    while live:
+        live = ctx.decode_step(1)
+    got, _ = ctx.decode_result(0)
+    ctx.decode_end()
+    assert prompt + got == ids
+    ctx.check_device_error()
+
+
+def test_bf16_8b_widths_logit_drift_vs_f32_oracle(model8):
+    """Where the tolerance comes from: on the same weights and window, the GPU path's
+    logit error against the bf16 oracle is smaller than the bf16 oracle's own distance
+    from the exact f32 computation (both reported)."""
+    cfg, ctx, bits, om = model8
+    rng = np.random.default_rng(5)
+    prompt = rng.integers(0, VOCAB - 2, size=PROMPT)
+    window = rng.integers(0, VOCAB - 2, size=WINDOW)
+    masks = np.sort(rng.permutation(WINDOW)[:64])
+    window[masks] = cfg.mask_token_id
+    filled = [i for i in range(WINDOW) if i not in set(masks.tolist())]
+    order = filled + masks.tolist()
+    tok = window[order]
+    pos = PROMPT + np.asarray(order)
+    ctx.reset_sequence(0)
+    ctx.prefill(0, prompt)
+    nf = len(filled)
+    lg = ctx.forward_with_positions([0], tok[None], pos[None], logit_row_begin=[nf],
+                                    logits_dtype=torch.float32).cpu().numpy()
+    ref, _ = om.forward_with_positions(tok, pos, om.prefill_cache(prompt),
+                                       logits_rows=slice(nf, WINDOW), round_logits=False)
+    of = OracleModel(cfg, bits, "f32")
+    exact, _ = of.forward_with_positions(tok, pos, of.prefill_cache(prompt),
+                                         logits_rows=slice(nf, WINDOW), round_logits=False)
+    e_gpu = np.abs(lg - ref)
+    e_bf16 = np.abs(ref - exact)
+    e_gpu_exact = np.abs(lg - exact)
+    print(f"\n[8B-widths bf16 logits, {LAYERS} layers] GPU vs bf16 oracle: max {e_gpu.max():.4f} "
+          f"mean {e_gpu.mean():.5f}; bf16 oracle vs f32 oracle: max {e_bf16.max():.4f} mean "
+          f"{e_bf16.mean():.5f}; GPU vs f32 oracle: max {e_gpu_exact.max():.4f} mean "
+          f"{e_gpu_exact.mean():.5f}")
+    assert e_gpu.max() <= LOGIT_MAX_ABS and e_gpu.mean() <= LOGIT_MEAN
+    assert e_gpu.mean() <= e_bf16.mean()
+    assert e_gpu_exact.mean() <= 1.25 * e_bf16.mean()
