@@ -720,6 +720,8 @@ def bench_serve_8b(args, rank, ws, local):
 
 # ----------------------------------------------------------------------------------
 PROMPT_8B, NEW_8B, WINDOW_8B = 512, 512, 96
+DECODE_8B_WORKLOAD = ("decode_8b: 8B-shape WeDLM, 512-token prompt, 512 new tokens, window 96, "
+                      "balanced preset (tau 0.8, lambda 0.05, cap 8), T 0")
 
 
 def balanced_params():
@@ -870,8 +872,7 @@ def bench_decode_8b(args, rank, ws, local):
         "ms_per_step": round(ms_max, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: random-init N(0,0.02^2) 8B-shape weights, uniform random prompt ids",
-        "config": {"workload": "decode_8b: 8B-shape WeDLM, 512-token prompt, 512 new tokens, "
-                               "window 96, balanced preset (tau 0.8, lambda 0.05, cap 8), T 0",
+        "config": {"workload": DECODE_8B_WORKLOAD,
                    "layers": 36, "hidden": 4096, "heads": "32/8", "head_dim": 128,
                    "ffn": 12288, "vocab": 151936, "window": WINDOW_8B,
                    "tokens_per_step": round(toks / args.steps, 3),
@@ -921,76 +922,100 @@ def bench_decode_8b(args, rank, ws, local):
     return line
 
 
-class OracleDecodeSample:
-    """A bounded sample of the decode step on the host cores, following the oracle: one
-    of the 36 8B-shape layers over a 96-row window against a 1024-token cache, the LM
-    head over the 96 rows for 1/8 of the vocabulary, and the C restatement of the
-    entropy / selection / argmax stage over 96 x 151936 logits.  ``run()`` returns the
-    extrapolated seconds of one full step (36 layers, whole vocabulary)."""
+def _host_normal(shape, std: float, seed: int, threads: int):
+    """N(0, std^2) f32 array drawn on `threads` host threads (numpy's generators release
+    the GIL while filling `out`), one independent stream per thread."""
+    import numpy as np
+    from concurrent.futures import ThreadPoolExecutor
+    out = np.empty(shape, np.float32)
+    flat = out.reshape(-1)
+    n = flat.size
+    ss = np.random.SeedSequence(seed).spawn(threads)
+    step = (n + threads - 1) // threads
 
-    def __init__(self, seed: int = 0):
+    def fill(i):
+        lo, hi = i * step, min(n, (i + 1) * step)
+        if lo < hi:
+            np.random.Generator(np.random.PCG64(ss[i])).standard_normal(
+                out=flat[lo:hi], dtype=np.float32)
+            flat[lo:hi] *= np.float32(std)
+
+    with ThreadPoolExecutor(threads) as ex:
+        list(ex.map(fill, range(threads)))
+    return out
+
+
+class HostDecodeRun:
+    """The reference's streaming decode step on the host cores, measured whole.
+
+    The oracle port of the reference path: the f32 forward of the full 8B-shape model
+    (``layers`` decoder layers, hidden 4096, 32/8 heads, SwiGLU 12288, vocabulary
+    151936, N(0, 0.02^2) weights, norm weights 1) with the LM head over all window rows
+    as ``causal_lm.rs:68-79`` computes it, the entropy / selection / greedy argmax of
+    ``sampler.rs`` and the loop of ``wedlm.rs:336-590`` (``oracle/decoder.py``), after
+    caching the 512-token prompt.  Every timed step is one real iteration of the loop
+    at the bench's cache lengths: nothing is sampled or extrapolated.  A step's time is
+    the interval between the starts of consecutive window forwards, which holds the
+    forward, the entropy pass, the selection and the commit / refill bookkeeping."""
+
+    def __init__(self, layers: int = 36, seed: int = 0):
+        import os as _os
         import numpy as np
-        from oracle.model import (OracleModel, WeDLMConfig, f32_to_bf16_bits, rope_tables,
-                                  weight_names)
-        cfg = WeDLMConfig.wedlm_8b()
-        one = WeDLMConfig(**{**cfg.to_dict(), "num_hidden_layers": 1,
-                             "vocab_size": 151936 // 8, "dtype": "float32"})
-        rng = np.random.default_rng(seed)
-        H = one.hidden_size
+        from oracle.model import OracleModel, WeDLMConfig, weight_names
+        cfg = WeDLMConfig(**{**WeDLMConfig.wedlm_8b().to_dict(), "num_hidden_layers": layers,
+                             "max_position_embeddings": 4096, "dtype": "float32"})
+        self.cfg = cfg
+        self.threads = _os.cpu_count() or 1
+        t0 = time.time()
         w = {}
-        for name, shape in weight_names(one):
-            if name.endswith("norm.weight"):
-                w[name] = np.ones(shape, np.float32)
-            elif name == "model.embed_tokens.weight":
-                w[name] = np.zeros((8, H), np.float32)
-            else:
-                w[name] = rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)
-        m = OracleModel.__new__(OracleModel)
-        m.cfg, m.dtype, m._r, m.w = one, "f32", (lambda a: np.asarray(a, np.float32)), w
-        m.cos, m.sin = rope_tables(one.head_dim, 2048, one.rope_theta, False)
-        self.m, self.w = m, w
-        L, S = 1024, 96
-        self.S = S
-        self.cache = (rng.standard_normal((8, L, 128), dtype=np.float32),
-                      rng.standard_normal((8, L, 128), dtype=np.float32))
-        self.h = rng.standard_normal((S, H), dtype=np.float32)
-        self.pos = L + rng.permutation(S)
-        self.logits = f32_to_bf16_bits(rng.standard_normal((S, 151936), dtype=np.float32) * 2.5)
-        self.desc = ""
+        for i, (name, shape) in enumerate(weight_names(cfg)):
+            w[name] = (np.ones(shape, np.float32) if name.endswith("norm.weight")
+                       else _host_normal(shape, 0.02, seed * 1000 + i, self.threads))
+        self.model = OracleModel(cfg, w, "f32")
+        self.setup_s = time.time() - t0
+        self.starts = []
+        self.model_forward = self.model.forward_with_positions
+        self.model.forward_with_positions = self._timed_forward
 
-    def run(self) -> float:
-        import numpy as np
-        from oracle import cbind
-        S = self.S
+    def _timed_forward(self, *a, **k):
+        self.starts.append(time.time())
+        return self.model_forward(*a, **k)
+
+    def run(self, steps: int, warmup: int):
+        """Cache the prompt, run the loop for warmup + steps iterations (and one more to
+        close the last interval); returns the seconds of each timed step."""
+        from oracle.decoder import OracleDecoder
+        from oracle.sampler import SamplingParams as OSP
+        prompt = make_prompt(PROMPT_8B, seed=0).tolist()
+        dec = OracleDecoder(self.model, self.cfg.mask_token_id, self.cfg.eos_token_id)
+        self.starts = []
         t0 = time.time()
-        h2, _ = self.m._layer(0, self.h, self.pos, self.cache, np.arange(S))
-        t_layer = time.time() - t0
-        t0 = time.time()
-        np.matmul(h2, self.w["lm_head.weight"].T)
-        t_head = (time.time() - t0) * 8
-        t0 = time.time()
-        cbind.entropy_select(self.logits, "bf16", 0.0, 0.8, 0.05, [0, S], list(range(S)), [8])
-        t_ent = time.time() - t0
-        self.desc = (f"1 of 36 layers ({t_layer:.3f} s) x 36 + LM head on 1/8 of the vocabulary "
-                     f"({t_head / 8:.3f} s) x 8 + entropy/selection over 96 x 151936 "
-                     f"({t_ent:.3f} s); numpy f32 with BLAS threads and the C restatement")
-        return 36 * t_layer + t_head + t_ent
+        # one committed token per step here (random-init entropy >> tau): max_new tokens
+        # take at least max_new + 1 iterations
+        dec.generate_streaming(prompt, warmup + steps + 1, WINDOW_8B,
+                               OSP(temperature=0.0, entropy_threshold=0.8,
+                                   distance_penalty=0.05, max_tokens_per_step=8))
+        self.total_s = time.time() - t0
+        st = self.starts
+        n = min(steps, len(st) - 1 - warmup)
+        return [st[warmup + i + 1] - st[warmup + i] for i in range(n)]
 
 
 def cpu_baseline_decode(budget_s: float):
-    import os as _os
-    smp = OracleDecodeSample()
-    smp.run()
-    steps, t0 = [], time.time()
-    while True:
-        steps.append(smp.run())
-        if time.time() - t0 >= budget_s:
-            break
+    """The reference arm's measurement as the GPU line's cpu_baseline: whole 36-layer
+    steps of the port (``HostDecodeRun``) after a one-step warm-up, about 2 s each on 16
+    cores: 3 of them, or fewer when the budget is below 6 s."""
+    run = HostDecodeRun()
+    n = 3 if budget_s >= 6.0 else 2
+    steps = run.run(steps=n, warmup=1)
     step = sum(steps) / len(steps)
-    return {"value": round(1.0 / step, 4), "unit": "committed tok/s", "cores": _os.cpu_count(),
+    return {"value": round(1.0 / step, 4), "unit": "committed tok/s", "cores": run.threads,
             "kind": "port",
-            "sample": smp.desc + f"; {len(steps)} samples, extrapolated {step:.2f} s per step, "
-                                 "1 committed token per step (random-init entropy >> tau)"}
+            "sample": f"{len(steps)} whole streaming steps of the 36-layer f32 port after a "
+                      f"512-token prompt (one window forward of 96 rows incl. the LM head over "
+                      f"all rows, entropy, selection, commit; {step:.2f} s per step), numpy with "
+                      f"{run.threads} BLAS threads; 1 committed token per step (random-init "
+                      f"entropy >> tau)"}
 
 
 def reference_attention(args, rank, ws):
@@ -1038,24 +1063,29 @@ def reference_attention(args, rank, ws):
 
 def reference_decode(args, rank, ws):
     """--impl reference for decode_8b: the reference's algorithm on the host cores (the
-    oracle port; the Rust crate cannot be built without cargo and candle), each step a
-    bounded sample extrapolated to a full 36-layer step."""
-    import os as _os
-    smp = OracleDecodeSample()
-    for _ in range(args.warmup):
-        smp.run()
-    steps = [smp.run() for _ in range(args.steps)]
-    desc = smp.desc
+    oracle port; the Rust crate cannot be built without cargo and candle).  Every step
+    is a whole streaming step of the 36-layer model (``HostDecodeRun``), timed as is.
+    ``--layers`` shrinks the model for quick contract checks only."""
+    layers = args.layers
+    run = HostDecodeRun(layers=layers)
+    steps = run.run(steps=args.steps, warmup=args.warmup)
     step = sum(steps) / len(steps)
     v = 1.0 / step
+    sample = (f"{len(steps)} whole streaming steps after {args.warmup} warm-up steps and the "
+              f"512-token prompt: {layers}-layer f32 port, one 96-row window forward incl. the "
+              f"LM head over all rows + entropy + selection + commit per step; numpy with "
+              f"{run.threads} BLAS threads (weights drawn in {run.setup_s:.1f} s, loop "
+              f"{run.total_s:.1f} s)")
+    workload = DECODE_8B_WORKLOAD if layers == 36 else \
+        DECODE_8B_WORKLOAD + f" [reduced to {layers} layers]"
     return {"metric": METRIC, "value": round(v, 4), "unit": "committed tok/s",
-            "impl": "reference", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+            "impl": "reference", "n_gpus": ws, "steps": len(steps), "warmup": args.warmup,
             "ms_per_step": round(step * 1e3, 1), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "decode_8b: 8B-shape WeDLM, window 96, balanced preset, T 0 "
-                                   "(one step = one window forward + entropy-select + commit)"},
+            "config": {"workload": workload, "layers": layers, "hidden": 4096, "heads": "32/8",
+                       "head_dim": 128, "ffn": 12288, "vocab": 151936, "window": WINDOW_8B},
             "cpu_baseline": {"value": round(v, 4), "unit": "committed tok/s",
-                             "cores": _os.cpu_count(), "kind": "port", "sample": desc},
+                             "cores": run.threads, "kind": "port", "sample": sample},
             "e2e": {"value": round(v, 4), "unit": "committed tok/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
 
