@@ -32,6 +32,8 @@ must commit exactly the lockstep trajectory's tokens.  Two parameter sets: tau 0
 (random-init entropy ~11.1 nats, so every step takes the fallback branch) and tau
 11.5 (the threshold branch: the rows within ~8 slots of the frontier pass, capped).
 """
+import os
+
 import numpy as np
 import pytest
 
@@ -227,3 +229,33 @@ def test_bf16_8b_widths_logit_drift_vs_f32_oracle(model8):
     assert e_gpu.max() <= LOGIT_MAX_ABS and e_gpu.mean() <= LOGIT_MEAN
     assert e_gpu.mean() <= e_bf16.mean()
     assert e_gpu_exact.mean() <= 1.25 * e_bf16.mean()
+
+
+@pytest.mark.parametrize("S", [96, 80, 64])
+def test_fused_layer_tail_equals_unfused_kernels(model8, S):
+    """The fused layer tail (one persistent kernel per layer after the attention, opt-in
+    with WEDLM_FUSED_TAIL=1) keeps the stream-K schedule, slot layout and arithmetic of
+    the stand-alone GEMM and consumer kernels, so with the same GEMM plans (one weight
+    tile per unit, which the fused tail always uses) the two forwards agree bit for bit.
+    Windows of 80 and 96 rows take the fused path; 64 rows does not, and must agree
+    trivially."""
+    cfg, ctx, bits, om = model8
+    rng = np.random.default_rng(S)
+    prompt = rng.integers(0, VOCAB - 2, size=PROMPT)
+    tok = rng.integers(0, VOCAB - 2, size=S)
+    tok[S // 3:] = cfg.mask_token_id
+    pos = PROMPT + rng.permutation(S)
+    out = {}
+    for mode in ("0", "1"):
+        os.environ["WEDLM_FUSED_TAIL"] = mode
+        os.environ["WEDLM_GEMM_NB"] = "1"
+        try:
+            ctx.reset_sequence(0)
+            ctx.prefill(0, prompt)
+            out[mode] = ctx.forward_with_positions([0], tok[None], pos[None], logit_row_begin=[S // 3],
+                                                   logits_dtype=torch.float32).clone()
+            ctx.check_device_error()
+        finally:
+            os.environ.pop("WEDLM_FUSED_TAIL", None)
+            os.environ.pop("WEDLM_GEMM_NB", None)
+    assert torch.equal(out["0"], out["1"]), (out["0"] - out["1"]).abs().max().item()

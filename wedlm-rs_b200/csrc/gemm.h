@@ -69,7 +69,8 @@ struct GemmPlan {
 };
 
 // bf16 tcgen05 path (K % 64 == 0).
-GemmPlan plan_gemm_tc(int M, int N, int K, bool dual, int num_sms);
+// force_nb = 1 or 2 fixes the weight tiles per stream-K unit (0: chosen by size).
+GemmPlan plan_gemm_tc(int M, int N, int K, bool dual, int num_sms, int force_nb = 0);
 Status run_gemm_tc(const GemmArgs& a, const GemmPlan& g, float* ws, unsigned* counters, int* err,
                    cudaStream_t st);
 void forget_tensor_maps();
@@ -143,6 +144,24 @@ __device__ __forceinline__ float4 ps_sum4_nb(const PsTile& t) {
 #pragma unroll
   for (int k = 0; k < B; ++k)
     u[k] = __ldcg(reinterpret_cast<const float4*>(t.base + (k < t.count ? k : 0) * t.stride));
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int k = 0; k < B; ++k)
+    if (k < t.count) {
+      s.x += u[k].x; s.y += u[k].y; s.z += u[k].z; s.w += u[k].w;
+    }
+  return s;
+}
+
+// Same sum with each of up to B loads predicated on the contributor count (no redundant
+// requests), all issued before the adds; the additions run in the same order as ps_sum4.
+template <int B>
+__device__ __forceinline__ float4 ps_sum4_pred(const PsTile& t) {
+  if (t.count > B) return ps_sum4(t);
+  float4 u[B];
+#pragma unroll
+  for (int k = 0; k < B; ++k)
+    if (k < t.count) u[k] = __ldcg(reinterpret_cast<const float4*>(t.base + k * t.stride));
   float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
   for (int k = 0; k < B; ++k)

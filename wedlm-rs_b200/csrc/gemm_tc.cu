@@ -31,6 +31,7 @@
 
 #include "gemm.h"
 #include "sm100.cuh"
+#include "tc_epilogue.cuh"
 
 namespace wedlm {
 
@@ -172,38 +173,6 @@ __device__ __forceinline__ Seg segment_at(long it, long end, int kb_total) {
   s.it1 = end < unit_end ? end : unit_end;
   s.full = (it == (long)s.unit * kb_total) && (s.it1 == unit_end);
   return s;
-}
-
-// Epilogue transpose of one accumulator chunk.  TMEM lane r (weight row rr + r) holds w
-// consecutive tokens (w = 32 or 16); through the warp's [32][33] shared buffer each lane
-// takes 8 consecutive weight rows, (lane % 4) * 8 .. + 7, of the four tokens
-// i * 8 + lane / 4 (i = 0..3), so that four lanes cover one token's 32 rows and the
-// global stores are whole 128-byte (f32) or 64-byte (bf16) runs.  Conflict-free: bank
-// (token + row) % 32 differs across the warp in both phases.
-__device__ __forceinline__ void epi_transpose(uint32_t taddr, int w, float* tb, int lane,
-                                              float (&o)[4][8]) {
-  float v[32];
-  if (w == 32) {
-    tmem_ld32(taddr, v);
-  } else {
-    float h[16];
-    tmem_ld16(taddr, h);
-#pragma unroll
-    for (int j = 0; j < 16; ++j) v[j] = h[j];
-#pragma unroll
-    for (int j = 16; j < 32; ++j) v[j] = 0.f;
-  }
-#pragma unroll
-  for (int j = 0; j < 32; ++j) tb[j * 33 + lane] = v[j];
-  __syncwarp();
-  const int r0 = (lane & 3) * 8;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int tl = i * 8 + (lane >> 2);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) o[i][e] = tb[tl * 33 + r0 + e];
-  }
-  __syncwarp();
 }
 
 // weight tiles present in unit u (the last group may hold fewer than nb)
@@ -646,7 +615,7 @@ PartialSet partial_set(const GemmPlan& g, const float* slots, bool dual) {
   return ps;
 }
 
-GemmPlan plan_gemm_tc(int M, int N, int K, bool dual, int num_sms) {
+GemmPlan plan_gemm_tc(int M, int N, int K, bool dual, int num_sms, int force_nb) {
   GemmPlan g;
   // Many token rows (prefill chunks, batched serving): the GEMM is tensor-bound and its
   // operands stream from L2.  Each unit then takes 256 token rows and two weight tiles
@@ -676,8 +645,9 @@ GemmPlan plan_gemm_tc(int M, int N, int K, bool dual, int num_sms) {
   if (const char* e = getenv("WEDLM_GEMM_NB_MB")) big_mb = atol(e);
   const bool big = (long)N * K * 2 >= big_mb * 1024 * 1024;
   int nb = (!dual && ((g.tok_tile <= 128 && big) || wide) && g.n_tiles >= 2) ? 2 : 1;
-  if (const char* e = getenv("WEDLM_GEMM_NB")) {
-    const int f = atoi(e);
+  const char* nb_env = getenv("WEDLM_GEMM_NB");
+  if (force_nb > 0 || nb_env) {
+    const int f = force_nb > 0 ? force_nb : atoi(nb_env);
     if (f == 1) nb = 1;
     if (f == 2 && !dual && g.tok_tile <= 128 && g.n_tiles >= 2) nb = 2;
   }

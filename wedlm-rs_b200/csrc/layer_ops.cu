@@ -7,6 +7,7 @@
 // back; RoPE uses cos/sin tables rounded to the model dtype (rope.rs:94-95) and rounds
 // its output.
 #include "layer_ops.h"
+#include "layer_ops_dev.cuh"
 
 #include <algorithm>
 
@@ -16,7 +17,7 @@ namespace {
 
 template <typename T>
 __device__ __forceinline__ T rnd(float v) {
-  return from_f32<T>(v);
+  return rnd_to<T>(v);
 }
 
 // ---- embedding -------------------------------------------------------------------
@@ -70,96 +71,18 @@ __global__ void rmsnorm_kernel(const T* __restrict__ x, long ldx, const float* _
 }
 
 // ---- QK-norm + RoPE + KV append ------------------------------------------------------
-// One warp per (row, head) over the q, k and v heads of the fused QKV output.  Head
-// dim d = 32 * E; lane holds elements lane*E .. lane*E+E-1; the rotate-half partner of
-// element i (i +/- d/2) sits in lane ^ 16 at the same slot.
+// One warp per (row, head) over the q, k and v heads of the fused QKV output
+// (rope_kv_item, layer_ops_dev.cuh).
 template <typename T, int E>
 __global__ void rope_kv_kernel(RopeKvArgs a, PartialSet ps_val) {
   pdl_trigger();
   pdl_wait();
-  if (a.qkv_partials != nullptr) a.qkv_partials = &ps_val;
   const int warps = blockDim.x >> 5;
   const int gw = blockIdx.x * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   const int heads = a.nh + 2 * a.nkv;
   if (gw >= a.rows * heads) return;
-  const int r = gw / heads, hh = gw % heads;
-  const int d = 32 * E;
-  float x[E];
-  if (a.qkv_partials != nullptr) {
-    // projection output rounded to the model dtype, as the reference's Linear returns it
-    if (E % 4 == 0) {
-#pragma unroll
-      for (int e = 0; e < E; e += 4) {
-        const PsTile t = ps_tile(*a.qkv_partials, r, hh * d + lane * E + e, 0);
-        const float4 v = ps_sum4_nb<8>(t);
-        x[e] = to_f32(rnd<T>(v.x));
-        x[e + 1] = to_f32(rnd<T>(v.y));
-        x[e + 2] = to_f32(rnd<T>(v.z));
-        x[e + 3] = to_f32(rnd<T>(v.w));
-      }
-    } else {
-#pragma unroll
-      for (int e = 0; e < E; ++e)
-        x[e] = to_f32(rnd<T>(ps_sum(*a.qkv_partials, r, hh * d + lane * E + e, 0)));
-    }
-  } else {
-    const T* src = reinterpret_cast<const T*>(a.qkv) + (long)r * a.ld_qkv + (long)hh * d;
-#pragma unroll
-    for (int e = 0; e < E; ++e) x[e] = to_f32(src[lane * E + e]);
-  }
-  const bool is_q = hh < a.nh, is_k = !is_q && hh < a.nh + a.nkv;
-  if (is_q || is_k) {
-    if (a.qk_norm) {
-      const float* w = is_q ? a.q_norm : a.k_norm;
-      float ss = 0.f;
-#pragma unroll
-      for (int e = 0; e < E; ++e) ss = fmaf(x[e], x[e], ss);
-      ss = warp_sum(ss);
-      const float denom = sqrtf(ss / (float)d + a.eps);
-#pragma unroll
-      for (int e = 0; e < E; ++e) x[e] = to_f32(rnd<T>((x[e] / denom) * w[lane * E + e]));
-    }
-    const int pos = a.positions[r];
-    const float* cs = a.cos + (long)pos * (d / 2);
-    const float* sn = a.sin + (long)pos * (d / 2);
-    float y[E];
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-      const float p = __shfl_xor_sync(0xffffffffu, x[e], 16);
-      const int fi = (lane & 15) * E + e;
-      const float c = cs[fi], s = sn[fi];
-      y[e] = lane < 16 ? x[e] * c - p * s : x[e] * c + p * s;
-    }
-#pragma unroll
-    for (int e = 0; e < E; ++e) x[e] = to_f32(rnd<T>(y[e]));
-  }
-  if (is_q) {
-    // group-major q: [nkv][rows * group][d], row index (r * group + h % group)
-    const int g = hh / a.group, hi = hh % a.group;
-    T* dst = reinterpret_cast<T*>(a.q_out) +
-             (((long)g * a.rows + r) * a.group + hi) * d;
-#pragma unroll
-    for (int e = 0; e < E; ++e) dst[lane * E + e] = rnd<T>(x[e]);
-    return;
-  }
-  // K / V into the paged cache at position dst_pos[r] of sequence row_seq[r]
-  const int kvh = is_k ? hh - a.nh : hh - a.nh - a.nkv;
-  const int seq = a.row_seq[r];
-  const int tpos = a.dst_pos[r];
-  const int page = a.page_table[(long)seq * a.pages_per_seq + tpos / a.page_size];
-  const int off = tpos % a.page_size;
-  const long page_base = (((long)a.layer * a.num_pages + page) * a.nkv + kvh) * (long)a.page_size * d;
-  if (is_k) {
-    T* dst = reinterpret_cast<T*>(a.kcache) + page_base + (long)off * d;
-#pragma unroll
-    for (int e = 0; e < E; ++e) dst[lane * E + e] = rnd<T>(x[e]);
-  } else {
-    // V stored transposed within a page: [d][page_size]
-    T* dst = reinterpret_cast<T*>(a.vcache) + page_base + off;
-#pragma unroll
-    for (int e = 0; e < E; ++e) dst[(long)(lane * E + e) * a.page_size] = rnd<T>(x[e]);
-  }
+  rope_kv_item<T, E>(a, a.qkv_partials != nullptr ? &ps_val : nullptr, gw, lane);
 }
 
 // ---- attention on CUDA cores (f32 models) -------------------------------------------
@@ -279,31 +202,12 @@ resid_norm_kernel(__nv_bfloat16* h, PartialSet ps, int has_ps, const float* __re
   }
 }
 
-// ---- SwiGLU from the gate/up partials ---------------------------------------------------
+// ---- SwiGLU from the gate/up partials (swiglu_range, layer_ops_dev.cuh) -------------
 __global__ void swiglu_kernel(PartialSet ps, int rows, int I, __nv_bfloat16* act) {
   pdl_trigger();
   pdl_wait();
-  const long n4 = (long)rows * I / 4;
-  for (long e4 = blockIdx.x * (long)blockDim.x + threadIdx.x; e4 < n4; e4 += (long)gridDim.x * blockDim.x) {
-    const long e = e4 * 4;
-    const int r = (int)(e / I), j = (int)(e % I);
-    const PsTile tg = ps_tile(ps, r, j, 0), tu = ps_tile(ps, r, j, 1);
-    const float4 g4 = ps_sum4_nb<4>(tg);
-    const float4 u4 = ps_sum4_nb<4>(tu);
-    const float gs[4] = {g4.x, g4.y, g4.z, g4.w}, us[4] = {u4.x, u4.y, u4.z, u4.w};
-    float y[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float g = __bfloat162float(__float2bfloat16_rn(gs[k]));
-      const float u = __bfloat162float(__float2bfloat16_rn(us[k]));
-      const float sg = __bfloat162float(__float2bfloat16_rn(g / (1.f + __expf(-g))));
-      y[k] = sg * u;
-    }
-    const __nv_bfloat162 a = __floats2bfloat162_rn(y[0], y[1]);
-    const __nv_bfloat162 b = __floats2bfloat162_rn(y[2], y[3]);
-    *reinterpret_cast<uint2*>(act + e) =
-        make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
-  }
+  swiglu_range(ps, rows, I, act, blockIdx.x * (long)blockDim.x + threadIdx.x,
+               (long)gridDim.x * blockDim.x);
 }
 
 }  // namespace

@@ -15,6 +15,7 @@
 #include <cstring>
 #include <string>
 
+#include "layer_fused.h"
 #include "model.h"
 
 namespace wedlm {
@@ -421,6 +422,7 @@ void model_destroy(wedlm_ctx* ctx) {
   cudaFree(m->attn);
   cudaFree(m->act);
   cudaFree(m->slots);
+  cudaFree(m->sync);
   cudaFree(m->d_meta);
   if (m->h_meta) cudaFreeHost(m->h_meta);
   cudaFree(m->attn_ws);
@@ -635,7 +637,86 @@ Status model_forward(wedlm_ctx* ctx, const std::vector<SeqSlice>& seqs, const in
     return s;
   };
 
-  if (tc) {
+  // bf16 windows of up to 96 rows: after each attention, one persistent kernel runs the
+  // rest of the layer and the next layer's QKV projection and RoPE (layer_fused.cu)
+  long fused_slots = 0;
+  const bool fused = tc && fused_tail_supported(R, m->H, m->I, m->qdim, m->qkvdim, m->d,
+                                                ctx->num_sms, &fused_slots);
+  if (fused) {
+    if (fused_slots > m->slot_floats) {
+      WEDLM_CUDA_TRY(cudaStreamSynchronize(st));
+      cudaFree(m->slots);
+      m->slots = nullptr;
+      m->slot_floats = 0;
+      WEDLM_CUDA_TRY(cudaMalloc(&m->slots, fused_slots * sizeof(float)));
+      m->slot_floats = fused_slots;
+    }
+    if (!m->sync) {
+      m->sync_count = m->nlayers * 16;
+      WEDLM_CUDA_TRY(cudaMalloc(&m->sync, m->sync_count * sizeof(unsigned)));
+    }
+    WEDLM_CUDA_TRY(cudaMemsetAsync(m->sync, 0, m->sync_count * sizeof(unsigned), st));
+  }
+  const double fused_bytes =
+      (double)es * ((double)m->H * m->qdim + 2.0 * m->I * m->H + (double)m->H * m->I +
+                    (double)m->qkvdim * m->H + (double)R * (m->qdim + 2.0 * m->H + m->I));
+  const double fused_flops =
+      2.0 * R * ((double)m->H * m->qdim + 3.0 * m->I * m->H + (double)m->qkvdim * m->H);
+
+  if (tc && fused) {
+    // embed -> norm -> QKV of layer 0 -> RoPE; then per layer: attention, fused tail
+    PartialSet ps;
+    int ph = prof_begin(ctx, st);
+    WEDLM_TRY(other(run_resid_norm(m->h, nullptr, m->layers[0].ln1, R, m->H, m->eps, m->xn, st),
+                    ph, norm_bytes));
+    WEDLM_TRY(gemm(m->xn, H, m->layers[0].wqkv, nullptr, m->qkvdim, m->H, EPI_STORE_BF16, nullptr,
+                   0, nullptr, 0, R, &ps));
+    rk.layer = 0;
+    rk.q_norm = m->layers[0].qn;
+    rk.k_norm = m->layers[0].kn;
+    rk.qkv_partials = &ps;
+    ph = prof_begin(ctx, st);
+    WEDLM_TRY(other(run_rope_kv(rk, m->dt, st), ph, rope_bytes));
+    for (int l = 0; l < m->nlayers; ++l) {
+      const LayerWeights& L = m->layers[l];
+      const bool last = l + 1 == m->nlayers;
+      WEDLM_TRY(attention(l));
+      FusedTailArgs ta;
+      ta.M = R;
+      ta.H = m->H;
+      ta.I = m->I;
+      ta.qdim = m->qdim;
+      ta.qkvdim = m->qkvdim;
+      ta.eps = m->eps;
+      ta.attn = m->attn;
+      ta.h = m->h;
+      ta.xn = m->xn;
+      ta.act = m->act;
+      ta.wo = L.wo;
+      ta.wgate = L.wgate;
+      ta.wup = L.wup;
+      ta.wdown = L.wdown;
+      ta.wqkv_next = last ? nullptr : m->layers[l + 1].wqkv;
+      ta.wo_next = last ? nullptr : m->layers[l + 1].wo;
+      ta.ln2 = L.ln2;
+      ta.ln_next = last ? m->final_norm : m->layers[l + 1].ln1;
+      ta.rope = rk;
+      ta.rope.layer = last ? l : l + 1;
+      ta.rope.q_norm = last ? L.qn : m->layers[l + 1].qn;
+      ta.rope.k_norm = last ? L.kn : m->layers[l + 1].kn;
+      ta.rope.qkv_partials = nullptr;
+      ta.slots = m->slots;
+      ta.slot_floats = m->slot_floats;
+      ta.sync = m->sync + (size_t)l * 16;
+      ta.err = err;
+      const double b = last ? fused_bytes - (double)es * m->qkvdim * m->H : fused_bytes;
+      const double f = last ? fused_flops - 2.0 * R * m->qkvdim * m->H : fused_flops;
+      ph = prof_begin(ctx, st);
+      Status sf = run_fused_tail(ta, ctx->num_sms, st);
+      prof_end(ctx, st, ph, WedlmProfiler::kGemm, b, f, 1);
+      WEDLM_TRY(sf);
+    }
+  } else if (tc) {
     // bf16: split-K partials are summed by the consuming kernel (RoPE / residual + norm /
     // SwiGLU); the residual add and the following RMSNorm are one kernel.
     PartialSet ps;

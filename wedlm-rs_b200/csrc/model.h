@@ -65,6 +65,8 @@ struct ModelState {
   size_t meta_ints = 0;
   float* slots = nullptr;  // split-K partial sets of the layer GEMMs (bf16)
   long slot_floats = 0;
+  unsigned* sync = nullptr;  // grid-wide dependency counters of the fused layer tails
+  int sync_count = 0;        // [layers][8]
   float* attn_ws = nullptr;
   long attn_ws_floats = 0;
   void* h_attn_staging = nullptr;

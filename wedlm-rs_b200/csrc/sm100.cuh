@@ -35,6 +35,17 @@ enum ErrCode : int {
   kErrAtSoftS = 23,
   kErrAtSoftO = 24,
   kErrAtSoftOLast = 25,
+  // fused layer tail: 32 + wait site; grid-wide dependency counter k: 48 + k
+  kErrFuEmptyW = 32,
+  kErrFuEmptyX = 33,
+  kErrFuFullW = 34,
+  kErrFuFullX = 35,
+  kErrFuAccEmpty = 36,
+  kErrFuAccFull = 37,
+  kErrFuDrainW = 38,
+  kErrFuDrainX = 39,
+  kErrFuStep = 40,
+  kErrFuGrid = 48,
 };
 
 __device__ __forceinline__ uint64_t global_ns() {
@@ -115,6 +126,40 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   return mbar_wait_for(bar, parity, err, code, kWaitNs);
 }
 
+// ---- grid-wide dependency counters (persistent kernels whose CTAs are co-resident) --
+// Release-add of one arrival: every write this thread observed (its own, and those of
+// the CTA's threads ordered before it by a barrier) is visible to a thread that
+// acquires the counter afterwards.
+__device__ __forceinline__ void counter_arrive(unsigned* c) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(c) : "memory");
+}
+__device__ __forceinline__ unsigned counter_acquire(const unsigned* c) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(c) : "memory");
+  return v;
+}
+// Bounded wait until *c >= target (kWaitNs of %globaltimer time); records `code` in
+// *err and returns false when it gives up.
+__device__ __forceinline__ bool counter_wait(const unsigned* c, unsigned target, int* err,
+                                             int code) {
+  if (counter_acquire(c) >= target) return true;
+  const uint64_t t0 = global_ns();
+  // poll with a short back-off: ~300 pollers (two per SM) on one L2 line must not crowd
+  // out the loads of the threads doing the work being waited for
+  for (uint32_t i = 0;; ++i) {
+    __nanosleep(128);
+    if (counter_acquire(c) >= target) return true;
+    if ((i & 31u) == 31u && global_ns() - t0 > kWaitNs) break;
+  }
+  if (err) atomicCAS(err, 0, code);
+  return false;
+}
+// Orders this thread's generic-proxy view of global memory with its later async-proxy
+// (TMA / bulk copy) accesses.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // ---- TMA -------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
@@ -150,6 +195,12 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
   return p;
+}
+// 16-byte store with an L2 eviction-priority hint (policy from createpolicy).
+__device__ __forceinline__ void st_v4_hint(float* p, float4 v, uint64_t policy) {
+  asm volatile("st.global.L2::cache_hint.v4.f32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(p), "f"(v.x),
+               "f"(v.y), "f"(v.z), "f"(v.w), "l"(policy)
+               : "memory");
 }
 __device__ __forceinline__ uint64_t policy_evict_last() {
   uint64_t p;
