@@ -51,16 +51,13 @@ def peaks():
         return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
 
 
-def profile_traffic(name: str, key: str = "traffic_bytes_per_launch"):
-    """DRAM bytes recorded by an ncu capture summary under profiles/ (``key:`` line)."""
-    p = os.path.join(ROOT, "profiles", name)
+def profile_traffic(name: str):
+    """DRAM bytes of one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum), from
+    the machine-readable record profiles/dram_traffic.json; None when absent."""
     try:
-        for line in open(p):
-            if line.startswith(key + ":"):
-                return float(line.split(":", 1)[1].strip())
-    except OSError:
-        pass
-    return None
+        return float(json.load(open(os.path.join(ROOT, "profiles", "dram_traffic.json")))[name]["bytes"])
+    except (OSError, KeyError, ValueError, TypeError):
+        return None
 
 
 class ClockSampler:
@@ -384,7 +381,7 @@ def bench_entropy_select(args, rank, ws, local):
         "gpu_launches": args.steps,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / hbm, 4),
-                     "traffic": profile_traffic("entropy_select_c2.md") if nseq == 64 else None,
+                     "traffic": profile_traffic("entropy_select_c2") if nseq == 64 else None,
                      "kernel": "entropy_select_kernel<bf16>"},
     }
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
@@ -621,7 +618,7 @@ def bench_block_attention(args, rank, ws, local):
             "gpu_launches": args.steps * 2,
             "roofline": {"bound": "tensor", "achieved": top["TFLOPs"], "peak": tflops_peak,
                          "peak_kind": peak_kind, "unit": "TFLOP/s", "frac": top["frac_tensor"],
-                         "traffic": profile_traffic("attention_tc_block_8192.md"),
+                         "traffic": profile_traffic("attention_tc_block_8192"),
                          "kernel": "attention_tc_kernel + attention_combine_kernel"}}
 
 
@@ -893,7 +890,7 @@ def bench_decode_8b(args, rank, ws, local):
         "roofline": {"bound": "hbm", "achieved": round(gemm_gbs, 1) if gemm_gbs else None,
                      "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s",
                      "frac": round(gemm_gbs / hbm, 4) if gemm_gbs else None,
-                     "traffic": profile_traffic("gemm_tc_decode_8b.md", "traffic_bytes_per_step"),
+                     "traffic": profile_traffic("gemm_tc_decode_8b"),
                      "per": "decode step (all GEMM-class launches of one step)",
                      "kernel": "gemm_tc_kernel (+ shared-tile reduce): QKV/O/gate-up/down/LM head",
                      "launches_per_step": round(g["launches"] / max(args.profile_steps, 1), 1),
