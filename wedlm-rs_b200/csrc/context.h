@@ -19,7 +19,7 @@ struct Comm;
 // Optional per-kernel-class timing with CUDA events on the launching stream
 // (enabled around a measured region; the events are recorded between launches).
 struct WedlmProfiler {
-  enum { kGemm = 0, kAttention = 1, kEntropy = 2, kOther = 3, kClasses = 4 };
+  enum { kGemm = 0, kAttention = 1, kEntropy = 2, kOther = 3, kComm = 4, kClasses = 5 };
   bool on = false;
   std::vector<cudaEvent_t> ev;
   struct Rec {

@@ -250,7 +250,10 @@ Status sharded_select(wedlm_ctx* ctx, DecodeSession* S, EntropyArgs& A, int nin,
   g[1].recv = S->shdr + 4;
   g[1].count = 4;
   g[1].dtype = kCommInt32;
-  WEDLM_TRY(comm_all_gather(c, g, 2, st));
+  int pc = prof_begin(ctx, st);
+  Status sg = comm_all_gather(c, g, 2, st);
+  prof_end(ctx, st, pc, WedlmProfiler::kComm, (double)n * (g[0].count * m->esz + 16), 0, 0);
+  WEDLM_TRY(sg);
 
   WEDLM_TRY(model_lm_head(ctx, S->hrecv, m->H, rows, S->slogits, m->dt, st));
 
@@ -270,7 +273,10 @@ Status sharded_select(wedlm_ctx* ctx, DecodeSession* S, EntropyArgs& A, int nin,
   gp.recv = S->precv;
   gp.count = (size_t)rows * 4;
   gp.dtype = WEDLM_F32;
-  WEDLM_TRY(comm_all_gather(c, &gp, 1, st));
+  pc = prof_begin(ctx, st);
+  sg = comm_all_gather(c, &gp, 1, st);
+  prof_end(ctx, st, pc, WedlmProfiler::kComm, (double)n * gp.count * 4, 0, 0);
+  WEDLM_TRY(sg);
 
   if (A.rows > 0) {
     ph = prof_begin(ctx, st);

@@ -487,7 +487,7 @@ class Context:
         check(lib().wedlm_decode_end(self.h), self.h)
 
     # ---- profiling --------------------------------------------------------------------------
-    KERNEL_CLASSES = ("gemm", "attention", "entropy", "other")
+    KERNEL_CLASSES = ("gemm", "attention", "entropy", "other", "comm")
 
     def profile_enable(self, on: bool = True) -> None:
         check(lib().wedlm_profile_enable(self.h, 1 if on else 0), self.h)
