@@ -14,9 +14,12 @@
 //                                          the cache stores V transposed within a page)
 // Both accumulators have TMEM lane = query row, so the thread that owns a query row does
 // its online softmax, rescales its O row when the running max grows, and writes it out.
-// Warp roles: warp 0 TMA producer (Q once, K/V chunks through a 2-stage ring), warp 1
-// TMEM allocator + MMA issuer, warps 2..9 softmax / correction / epilogue, two threads
-// per query row (64 key columns and 64 O columns each).
+// Warp roles: warp 0 TMA producer of Q (once) and the K chunks, warp 10 TMA producer of
+// the V chunks (K and V have rings of their own: a K stage is free as soon as its QK^T
+// has run, long before the PV of the same chunk, so K(i+2) loads while the softmax of
+// chunk i runs), warp 1 TMEM allocator + MMA issuer, warps 2..9 softmax / correction /
+// epilogue, two threads per query row (64 key columns and 64 O columns each).  S has two
+// TMEM buffers, so QK^T of chunk i+1 runs while the softmax reads chunk i.
 // A work item covering only part of the keys writes (m, l, O) partials; a combine
 // kernel merges them (flash-decoding split-KV).
 #include <cudaTypedefs.h>
@@ -37,7 +40,7 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kThreadsAT = 320;   // warp 0 TMA, warp 1 MMA, warps 2..9 softmax
+constexpr int kThreadsAT = 352;   // warp 0 TMA Q/K, warp 1 MMA, warps 2..9 softmax, warp 10 TMA V
 constexpr int kSoftThreads = 256;
 constexpr int kQT = 128;        // query rows per tile
 constexpr int kKC = 128;        // keys per chunk (two 64-key pages)
@@ -101,18 +104,24 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  // layout: Q (2 blocks) | stage s: K (2 blocks), V (2 blocks) | P (2 blocks) | barriers
+  // layout: Q (2 blocks) | K stages (2 blocks each) | V stages (2 blocks each) | P (2 blocks)
+  //         | barriers (<= 14) | TMEM slot | ranks
   uint8_t* sQ = smem;
-  uint8_t* sKV = sQ + 2 * kBlk;
-  uint8_t* sP = sKV + kStages * 4 * kBlk;
+  uint8_t* sK = sQ + 2 * kBlk;
+  uint8_t* sV = sK + kStages * 2 * kBlk;
+  uint8_t* sP = sV + kStages * 2 * kBlk;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kBlk);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = kv_full + kStages;
-  uint64_t* s_full = kv_empty + kStages;
-  uint64_t* p_full = s_full + 1;
+  uint64_t* k_full = bars + 1;           // [kStages]
+  uint64_t* k_empty = k_full + kStages;  // [kStages]
+  uint64_t* v_full = k_empty + kStages;  // [kStages]
+  uint64_t* v_empty = v_full + kStages;  // [kStages]
+  uint64_t* s_full = v_empty + kStages;  // [2]: S buffers
+  uint64_t* p_full = s_full + 2;
   uint64_t* o_done = p_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 1);
+  // fixed offsets after the barriers, so that s_krank (read as int4) stays 16-byte
+  // aligned: slot at byte 112, ranks from byte 128
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
   int* s_rank = reinterpret_cast<int*>(tmem_slot + 4);  // window ranks of sequence b
   int* s_krank = s_rank + 4096;                          // key ranks of the current chunk
   float* s_red = reinterpret_cast<float*>(s_krank + kKC);  // [4][128]: row max / sum halves
@@ -128,56 +137,70 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(kv_full + s, 1);
-      mbar_init(kv_empty + s, 1);
+      mbar_init(k_full + s, 1);
+      mbar_init(k_empty + s, 1);
+      mbar_init(v_full + s, 1);
+      mbar_init(v_empty + s, 1);
     }
     mbar_init(s_full, 1);
+    mbar_init(s_full + 1, 1);
     mbar_init(p_full, 1);
     mbar_init(o_done, 1);
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, 256);
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + 128;
+  // two S buffers (S of chunk i in buffer i % 2, so that the next chunk's QK^T runs while
+  // the softmax reads this one) and the O accumulator
+  const uint32_t tS = tmem, tO = tmem + 256;
 
-  if (warp == 0) {
+  if (warp == 0 || warp == 10) {
     if (lane == 0) {
-      // ---------------- TMA producer ----------------
-      tma_prefetch_desc(&tmQ);
-      tma_prefetch_desc(&tmK);
-      tma_prefetch_desc(&tmV);
-      // Q tile: rows (g * rows + row0) * group + t * 128 of the group-major q buffer
-      const int qrow = (g * p.rows + row0) * p.group + w.t * kQT;
-      mbar_arrive_expect_tx(q_full, 2 * kBlk);
-      tma_load_2d(sQ, &tmQ, q_full, 0, qrow);
-      tma_load_2d(sQ + kBlk, &tmQ, q_full, 64, qrow);
+      // ---------------- TMA producers: Q and K (warp 0), V (warp 10) ----------------
+      const bool kside = warp == 0;
+      uint64_t* full = kside ? k_full : v_full;
+      uint64_t* empty = kside ? k_empty : v_empty;
+      if (kside) {
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmK);
+        // Q tile: rows (g * rows + row0) * group + t * 128 of the group-major q buffer
+        const int qrow = (g * p.rows + row0) * p.group + w.t * kQT;
+        mbar_arrive_expect_tx(q_full, 2 * kBlk);
+        tma_load_2d(sQ, &tmQ, q_full, 0, qrow);
+        tma_load_2d(sQ + kBlk, &tmQ, q_full, 64, qrow);
+      } else {
+        tma_prefetch_desc(&tmV);
+      }
       int issued = 0;
       for (int i = 0; i < nchunks; ++i) {
         const int s = i % kStages;
         const uint32_t ph = (uint32_t)(i / kStages) & 1u;
-        if (!mbar_wait(kv_empty + s, ph ^ 1u, p.err, kErrAtKvEmpty)) break;
+        if (!mbar_wait(empty + s, ph ^ 1u, p.err, kErrAtKvEmpty)) break;
         issued = i + 1;
-        uint8_t* st = sKV + s * 4 * kBlk;
-        mbar_arrive_expect_tx(kv_full + s, 4 * kBlk);
+        uint8_t* st = (kside ? sK : sV) + s * 2 * kBlk;
+        mbar_arrive_expect_tx(full + s, 2 * kBlk);
         const int c = w.c0 + i;
         for (int pg = 0; pg < 2; ++pg) {
           const int page = p.page_table[(long)slot * p.pages_per_seq + 2 * c + pg];
-          const int krow = ((p.layer * p.num_pages + page) * p.nkv + g) * p.page_size;
-          // K: two d-halves (K-blocks), keys of page pg at rows 64 * pg
-          tma_load_2d(st + pg * (kBlk / 2), &tmK, kv_full + s, 0, krow);
-          tma_load_2d(st + kBlk + pg * (kBlk / 2), &tmK, kv_full + s, 64, krow);
-          // V^T page: [128 d rows x 64 keys] = K-block pg of the B operand
-          const int vrow = ((p.layer * p.num_pages + page) * p.nkv + g) * kD;
-          tma_load_2d(st + 2 * kBlk + pg * kBlk, &tmV, kv_full + s, 0, vrow);
+          if (kside) {
+            // K: two d-halves (K-blocks), keys of page pg at rows 64 * pg
+            const int krow = ((p.layer * p.num_pages + page) * p.nkv + g) * p.page_size;
+            tma_load_2d(st + pg * (kBlk / 2), &tmK, full + s, 0, krow);
+            tma_load_2d(st + kBlk + pg * (kBlk / 2), &tmK, full + s, 64, krow);
+          } else {
+            // V^T page: [128 d rows x 64 keys] = K-block pg of the B operand
+            const int vrow = ((p.layer * p.num_pages + page) * p.nkv + g) * kD;
+            tma_load_2d(st + pg * kBlk, &tmV, full + s, 0, vrow);
+          }
         }
       }
-      mbar_wait(q_full, 0, p.err, kErrAtDrainQ);
+      if (kside) mbar_wait(q_full, 0, p.err, kErrAtDrainQ);
       for (int s = 0; s < kStages && s < issued; ++s) {
         const int last = s + ((issued - 1 - s) / kStages) * kStages;
-        mbar_wait(kv_full + s, (uint32_t)(last / kStages) & 1u, p.err, kErrAtDrainKv);
+        mbar_wait(full + s, (uint32_t)(last / kStages) & 1u, p.err, kErrAtDrainKv);
       }
     }
   } else if (warp == 1) {
@@ -186,45 +209,51 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
       const uint32_t idesc = idesc_bf16_f32(128, 128);
       const uint32_t aq = smem_u32(sQ), ap = smem_u32(sP);
       bool ok = mbar_wait(q_full, 0, p.err, kErrAtMmaQ);
-      for (int i = 0; i < nchunks && ok; ++i) {
-        const int s = i % kStages;
-        if (!mbar_wait(kv_full + s, (uint32_t)(i / kStages) & 1u, p.err, kErrAtMmaKv)) break;
+      // O += P(j) . V(j), once the softmax has published P(j) and V(j) has landed
+      auto pv = [&](int j, int code) -> bool {
+        const int sv = j % kStages;
+        if (!mbar_wait(p_full, (uint32_t)j & 1u, p.err, code)) return false;
+        if (!mbar_wait(v_full + sv, (uint32_t)(j / kStages) & 1u, p.err, kErrAtMmaKv)) return false;
         tc_fence_after();
-        const uint32_t bk = smem_u32(sKV + s * 4 * kBlk);
-        if (i > 0) {
-          // O += P(i-1) . V(i-1)
-          if (!mbar_wait(p_full, (uint32_t)(i - 1) & 1u, p.err, kErrAtMmaP)) break;
-          tc_fence_after();
-          const int sp = (i - 1) % kStages;
-          const uint32_t bv = smem_u32(sKV + sp * 4 * kBlk + 2 * kBlk);
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            tc_mma_f16(tO, smem_desc_sw128(ap + (kk >> 2) * kBlk + (kk & 3) * 32),
-                       smem_desc_sw128(bv + (kk >> 2) * kBlk + (kk & 3) * 32), idesc,
-                       (i - 1) > 0 || kk > 0);
-          tc_commit(o_done);
-          tc_commit(kv_empty + sp);
-        }
-        // S = Q . K(i)^T
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          tc_mma_f16(tS, smem_desc_sw128(aq + (kk >> 2) * kBlk + (kk & 3) * 32),
-                     smem_desc_sw128(bk + (kk >> 2) * kBlk + (kk & 3) * 32), idesc, kk > 0);
-        tc_commit(s_full);
-      }
-      if (ok && nchunks > 0 &&
-          mbar_wait(p_full, (uint32_t)(nchunks - 1) & 1u, p.err, kErrAtMmaPLast)) {
-        tc_fence_after();
-        const int sp = (nchunks - 1) % kStages;
-        const uint32_t bv = smem_u32(sKV + sp * 4 * kBlk + 2 * kBlk);
+        const uint32_t bv = smem_u32(sV + sv * 2 * kBlk);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
           tc_mma_f16(tO, smem_desc_sw128(ap + (kk >> 2) * kBlk + (kk & 3) * 32),
                      smem_desc_sw128(bv + (kk >> 2) * kBlk + (kk & 3) * 32), idesc,
-                     (nchunks - 1) > 0 || kk > 0);
+                     j > 0 || kk > 0);
+        tc_commit(o_done);
+        tc_commit(v_empty + sv);
+        return true;
+      };
+      bool all_pv = nchunks > 0;  // every PV issued (each commits o_done once)
+      for (int i = 0; i < nchunks && ok; ++i) {
+        const int s = i % kStages;
+        if (!mbar_wait(k_full + s, (uint32_t)(i / kStages) & 1u, p.err, kErrAtMmaKv)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t bk = smem_u32(sK + s * 2 * kBlk);
+        // S(i) = Q . K(i)^T into S buffer i % 2, issued as soon as K(i) has landed, so it
+        // runs while the softmax works on S(i-1) (buffer i % 2 was freed when the softmax
+        // of chunk i - 2 published P, which this thread waited for before PV(i-2))
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          tc_mma_f16(tS + (uint32_t)((i & 1) * 128),
+                     smem_desc_sw128(aq + (kk >> 2) * kBlk + (kk & 3) * 32),
+                     smem_desc_sw128(bk + (kk >> 2) * kBlk + (kk & 3) * 32), idesc, kk > 0);
+        tc_commit(s_full + (i & 1));
+        tc_commit(k_empty + s);  // K(i) is read once QK^T(i) completes
+        if (i > 0 && !pv(i - 1, kErrAtMmaP)) {
+          ok = false;
+          break;
+        }
       }
-      tc_commit(o_done);
-      tc_commit(kv_empty + ((nchunks > 0 ? nchunks - 1 : 0) % kStages));
+      all_pv = all_pv && ok && pv(nchunks - 1, kErrAtMmaPLast);
+      // without a last PV (no chunk, or a wait gave up) one commit still lets the softmax
+      // warps' final o_done wait end; after a last PV, a second commit would complete the
+      // barrier's next phase and alias the parity they wait for
+      if (!all_pv) tc_commit(o_done);
     }
   } else {
     // ---------------- softmax / correction / epilogue (warps 2..9) ----------------
@@ -243,13 +272,13 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int i = 0; i < nchunks && ok; ++i) {
-      ok = mbar_wait(s_full, (uint32_t)i & 1u, p.err, kErrAtSoftS);
+      ok = mbar_wait(s_full + (i & 1), (uint32_t)(i >> 1) & 1u, p.err, kErrAtSoftS);
       tc_fence_after();
       const int kbase = (w.c0 + i) * kKC;
       // this half's 64 scores of the query row, after one TMEM wait; masked keys become
       // -inf (log2 units after the scale)
       float sv[64];
-      tmem_ld64(tS + lane_off + col0, sv);
+      tmem_ld64(tS + (uint32_t)((i & 1) * 128) + lane_off + col0, sv);
       float cm = -INFINITY;
       if (kbase + kKC <= L) {  // chunk inside the committed prefix: every key visible
 #pragma unroll
@@ -368,7 +397,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
