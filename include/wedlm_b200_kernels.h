@@ -89,7 +89,7 @@ WEDLM_API int wedlm_kernel_wait_probe(wedlm_ctx* ctx, int64_t limit_ns, int32_t*
 enum wedlm_kernel_class {
   WEDLM_KC_GEMM = 0,       /* projection GEMMs (tcgen05) incl. their shared-tile reduce */
   WEDLM_KC_ATTENTION = 1,  /* block attention incl. the split-KV combine               */
-  WEDLM_KC_ENTROPY = 2,    /* fused entropy-select                                      */
+  WEDLM_KC_ENTROPY = 2,    /* fused entropy-select and the T > 0 sampling kernels       */
   WEDLM_KC_OTHER = 3,      /* embedding, RMSNorm, RoPE/KV append, row gather            */
   WEDLM_KC_COMM = 4        /* NCCL all-gathers of the vocabulary-sharded decode (not
                               kernels of this library: counted as 0 launches)          */

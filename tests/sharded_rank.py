@@ -11,6 +11,12 @@ loop; the LM head and the entropy pass run sharded over all ranks.  Cases:
          context on the same GPU go to OUT_JSON.
   leave  both ranks run one sharded step; then rank 1 exits between steps and rank 0's
          next step must end with WEDLM_ERR_TIMEOUT within the communicator timeout.
+  sample       fp32 parity model at T > 0 (multinomial and nucleus), seeded per rank; the
+               ids go to OUT_JSON for the oracle check.
+  sample_bf16  1-layer bf16 model at T > 0 (multinomial and nucleus); the ids of the
+               sharded decode and of a whole-vocabulary context with the same seed.
+  mismatch     rank 0 asks for T = 0 and rank 1 for T > 0: both ranks' decode_begin must
+               refuse with WEDLM_ERR_INVALID_ARG, and a matching decode must then run.
 """
 import json
 import os
@@ -35,6 +41,16 @@ def params(tau, lam, cap):
     from wedlm_b200 import SamplingParams
     return SamplingParams(temperature=0.0, entropy_threshold=tau, distance_penalty=lam,
                           max_tokens_per_step=cap)
+
+
+# (temperature, top_p) of the T > 0 cases
+SAMPLE_MODES = {"multinomial": (0.8, 1.0), "nucleus": (1.0, 0.7)}
+
+
+def sample_params(T, top_p, tau, lam, cap):
+    from wedlm_b200 import SamplingParams
+    return SamplingParams(temperature=T, top_p=top_p, entropy_threshold=tau,
+                          distance_penalty=lam, max_tokens_per_step=cap)
 
 
 def c1_prompts(rank):
@@ -113,6 +129,55 @@ def main():
         # the context still runs work that needs no communicator
         ctx.check_device_error()
         res["context_usable"] = True
+        ctx.close()
+    elif case == "sample":
+        cfg = c1_config()
+        w = random_weights(cfg, seed=0, std=0.02)
+        ctx = shard_ctx(cfg, w, rank, nranks, 2, 256, 32)
+        ctx.comm_init(uid, rank, nranks, timeout_ms=60000)
+        win = 12 if rank == 0 else 8
+        res["window"] = win
+        for name, (T, top_p) in SAMPLE_MODES.items():
+            ctx.set_sampling_seed(77 + rank)
+            outs, steps = ctx.generate_streaming_batch(c1_prompts(rank), 24, win,
+                                                       sample_params(T, top_p, *C1_PARAMS))
+            res[name] = {"ids": [list(map(int, o)) for o in outs],
+                         "steps": [int(x) for x in steps]}
+        ctx.check_device_error()
+        ctx.close()
+    elif case == "sample_bf16":
+        from wedlm_b200 import Context
+        cfg = long_ctx_bf16_config()
+        w = random_weights(cfg, seed=3, std=0.02)
+        ctx = shard_ctx(cfg, w, rank, nranks, 1, 512, 32)
+        ctx.comm_init(uid, rank, nranks, timeout_ms=60000)
+        full = Context(to_model_config(cfg, max_block_tokens=32), max_seqs=1, max_ctx=512)
+        full.load_weights(w)
+        for name, (T, top_p) in SAMPLE_MODES.items():
+            prm = sample_params(T, top_p, 0.8, 0.05, 8)
+            ids = []
+            for c in (ctx, full):
+                c.set_sampling_seed(31 + rank)
+                outs, _ = c.generate_streaming_batch(bf16_prompts(rank), 32, 16, prm)
+                ids.append([list(map(int, o)) for o in outs])
+            res[name] = {"ids": ids[0], "ids_whole_vocab": ids[1]}
+        ctx.close()
+        full.close()
+    elif case == "mismatch":
+        from wedlm_b200 import WedlmError
+        cfg = c1_config()
+        w = random_weights(cfg, seed=0, std=0.02)
+        ctx = shard_ctx(cfg, w, rank, nranks, 1, 256, 32)
+        ctx.comm_init(uid, rank, nranks, timeout_ms=30000)
+        try:
+            ctx.decode_begin([0], c1_prompts(1), 8, 8,
+                             sample_params(0.7 * rank, 1.0, 0.8, 0.05, 8))
+            res["code"] = 0
+        except WedlmError as e:
+            res["code"] = e.code
+            res["message"] = str(e)
+        outs, _ = ctx.generate_streaming_batch(c1_prompts(1), 8, 8, params(0.8, 0.05, 8))
+        res["after"] = [list(map(int, o)) for o in outs]
         ctx.close()
     else:
         raise SystemExit(f"unknown case {case}")

@@ -19,7 +19,10 @@
 // LM-head rows and reduces them to per-row partials (max, sum of exponentials, entropy
 // sum, argmax), the partials are all-gathered, and each rank combines the shards for its
 // own rows and applies the commit rule.  Both gathers run on NCCL over NVLink; the ranks
-// step in lock step until no rank has a live sequence.
+// step in lock step until no rank has a live sequence.  At T > 0 the owners' draws travel
+// with the hidden rows, and the picked rows are sampled over the split vocabulary in
+// phases with a small all-gather after each (sample.cu, run_shard_sample), giving the
+// tokens a whole-vocabulary context gives.
 #include <algorithm>
 #include <cstring>
 #include <vector>
@@ -81,11 +84,20 @@ struct DecodeSession {
   void* slogits = nullptr;  // [nranks * rmax, vshard]
   float* psend = nullptr;   // [nranks * rmax, 4]
   float* precv = nullptr;   // [nranks, nranks * rmax, 4]
+  // T > 0 over the sharded vocabulary: the owners' draws of their mask rows (gathered
+  // with the hidden rows), the replicated per-row sampling state and the phase exchange.
+  uint8_t* xblock = nullptr;
+  float* usend = nullptr;             // [rmax]
+  float* urecv = nullptr;             // [nranks * rmax]
+  ShardSampleRow* sstate = nullptr;   // [nranks * rmax]
+  void* xsend = nullptr;              // shard_sample_xbytes
+  void* xrecv = nullptr;              // nranks * shard_sample_xbytes
 
   ~DecodeSession() {
     cudaFree(block);
     cudaFree(shdr);
     cudaFree(sblock);
+    cudaFree(xblock);
     if (h_in) cudaFreeHost(h_in);
     if (h_out) cudaFreeHost(h_out);
   }
@@ -98,8 +110,16 @@ void session_free(wedlm_ctx* ctx) {
 
 namespace {
 
+// The sampling mode as the ranks compare it: T and, for T > 0, top_p (bit patterns).
+void sampling_key(const wedlm_sampling_params& p, int* out) {
+  std::memcpy(&out[0], &p.temperature, 4);
+  const float tp = p.temperature > 0.f ? p.top_p : 0.f;
+  std::memcpy(&out[1], &tp, 4);
+}
+
 // Sharded session set-up (collective: every rank of the communicator calls it): agree on
-// the rows per rank of the gathered buffers and allocate them.
+// the rows per rank of the gathered buffers and on the sampling mode (every rank must run
+// the same collectives each step), and allocate the buffers.
 Status sharded_begin(wedlm_ctx* ctx, DecodeSession* S, cudaStream_t st) {
   ModelState* m = ctx->model;
   Comm* c = ctx->comm;
@@ -107,17 +127,26 @@ Status sharded_begin(wedlm_ctx* ctx, DecodeSession* S, cudaStream_t st) {
   WEDLM_CUDA_TRY(cudaMalloc(&S->shdr, sizeof(int) * 4 * (n + 1)));
   WEDLM_CUDA_TRY(cudaMemsetAsync(S->shdr, 0, sizeof(int) * 4 * (n + 1), st));
   S->h_in[0] = S->rows_cap;
-  WEDLM_CUDA_TRY(cudaMemcpyAsync(S->shdr, S->h_in, sizeof(int), cudaMemcpyHostToDevice, st));
+  sampling_key(S->prm, S->h_in + 1);
+  S->h_in[3] = 0;
+  WEDLM_CUDA_TRY(cudaMemcpyAsync(S->shdr, S->h_in, sizeof(int) * 4, cudaMemcpyHostToDevice, st));
   GatherPiece g;
   g.send = S->shdr;
   g.recv = S->shdr + 4;
-  g.count = 1;
+  g.count = 4;
   g.dtype = kCommInt32;
   WEDLM_TRY(comm_all_gather(c, &g, 1, st));
-  WEDLM_CUDA_TRY(cudaMemcpyAsync(S->h_out, S->shdr + 4, sizeof(int) * n, cudaMemcpyDeviceToHost, st));
+  WEDLM_CUDA_TRY(cudaMemcpyAsync(S->h_out, S->shdr + 4, sizeof(int) * 4 * n,
+                                 cudaMemcpyDeviceToHost, st));
   WEDLM_TRY(comm_sync(c, st));
   int rmax = 0;
-  for (int r = 0; r < n; ++r) rmax = std::max(rmax, S->h_out[r]);
+  for (int r = 0; r < n; ++r) {
+    rmax = std::max(rmax, S->h_out[4 * r]);
+    // every rank sees the same table, so every rank refuses together
+    if (S->h_out[4 * r + 1] != S->h_out[1] || S->h_out[4 * r + 2] != S->h_out[2])
+      return Status::err(WEDLM_ERR_INVALID_ARG,
+                         "the ranks of a sharded decode must use the same temperature and top_p");
+  }
   S->rmax = rmax;
   const size_t H = m->H, es = m->esz, rows = (size_t)n * rmax;
   auto up = [](size_t b) { return (b + 255) / 256 * 256; };
@@ -132,6 +161,18 @@ Status sharded_begin(wedlm_ctx* ctx, DecodeSession* S, cudaStream_t st) {
   S->precv = reinterpret_cast<float*>(S->sblock + b_hs + b_hr + b_lg + b_ps);
   // rows past a rank's mask rows are projected too: keep them finite
   WEDLM_CUDA_TRY(cudaMemsetAsync(S->hsend, 0, b_hs + b_hr, st));
+  if (S->prm.temperature > 0.f) {
+    const size_t b_us = up((size_t)rmax * 4), b_ur = up(rows * 4),
+                 b_st = up(rows * sizeof(ShardSampleRow)),
+                 b_x = up(shard_sample_xbytes((int)rows, rmax, S->prm.top_p < 1.f));
+    WEDLM_CUDA_TRY(cudaMalloc(&S->xblock, b_us + b_ur + b_st + b_x * (n + 1)));
+    S->usend = reinterpret_cast<float*>(S->xblock);
+    S->urecv = reinterpret_cast<float*>(S->xblock + b_us);
+    S->sstate = reinterpret_cast<ShardSampleRow*>(S->xblock + b_us + b_ur);
+    S->xsend = S->xblock + b_us + b_ur + b_st;
+    S->xrecv = S->xblock + b_us + b_ur + b_st + b_x;
+    WEDLM_CUDA_TRY(cudaMemsetAsync(S->xblock, 0, b_us + b_ur + b_st + b_x * (n + 1), st));
+  }
   S->sharded = true;
   return Status::ok();
 }
@@ -151,8 +192,6 @@ Status session_begin(wedlm_ctx* ctx, const std::vector<int>& slots, const int32_
   WEDLM_CHECK_ARG(prm.temperature >= 0.f && std::isfinite(prm.temperature),
                   "temperature must be >= 0");
   WEDLM_CHECK_ARG(prm.temperature == 0.f || prm.top_p > 0.f, "top_p must be > 0");
-  WEDLM_CHECK_ARG(prm.temperature == 0.f || !ctx->comm,
-                  "T > 0 sampling needs the whole vocabulary on the context (no communicator)");
   WEDLM_CHECK_ARG(n_prompt + max_new + window <= m->max_ctx, "prompt + generation exceed max_ctx");
   if (!ctx->comm && m->vshard != m->V)
     return Status::err(WEDLM_ERR_STATE,
@@ -200,7 +239,8 @@ Status session_begin(wedlm_ctx* ctx, const std::vector<int>& slots, const int32_
   S->rows_cap = B * window;
   S->nseq_cap = B;
   const size_t lbytes = ((size_t)S->rows_cap * m->vshard * m->esz + 255) / 256 * 256;
-  const size_t in_ints = (size_t)4 * B + 1 + S->rows_cap + 4;  // + the sharded step's header
+  // + the sharded step's header and draws
+  const size_t in_ints = (size_t)4 * B + 1 + S->rows_cap + 4 + S->rows_cap;
   const size_t out_ints = (size_t)3 * S->rows_cap + B;
   const int nranks = ctx->comm ? comm_size(ctx->comm) : 1;
   WEDLM_CUDA_TRY(cudaMalloc(&S->block, lbytes + (in_ints + B + out_ints) * 4 + 1024));
@@ -238,10 +278,28 @@ Status sharded_select(wedlm_ctx* ctx, DecodeSession* S, EntropyArgs& A, int nin,
   hdr[0] = A.nseq;
   hdr[1] = A.rows;
   hdr[2] = hdr[3] = 0;
+  const bool sample = S->prm.temperature > 0.f;
+  if (sample && A.rows > 0) {
+    // the owner's draw of each of its mask rows: (seed, session index, step, mask row),
+    // the key the whole-vocabulary sampler uses
+    const int nb = A.nseq;
+    const int* h_rows = S->h_in;
+    const int* h_ridx = S->h_in + nb + 1 + A.rows + nb;
+    const int* h_step = h_ridx + nb;
+    float* hu = reinterpret_cast<float*>(hdr + 4);
+    for (int k = 0; k < nb; ++k)
+      for (int i = h_rows[k]; i < h_rows[k + 1]; ++i)
+        hu[i] = sample_draw(ctx->sample_seed, (uint64_t)h_ridx[k], (uint64_t)h_step[k],
+                            (uint64_t)(i - h_rows[k]));
+  }
   WEDLM_CUDA_TRY(cudaMemcpyAsync(S->d_in, S->h_in, (size_t)(nin + 4) * 4, cudaMemcpyHostToDevice, st));
   S->h2d_bytes += (nin + 4) * 4;
+  if (sample && A.rows > 0) {
+    WEDLM_CUDA_TRY(cudaMemcpyAsync(S->usend, hdr + 4, (size_t)A.rows * 4, cudaMemcpyHostToDevice, st));
+    S->h2d_bytes += A.rows * 4;
+  }
 
-  GatherPiece g[2];
+  GatherPiece g[3];
   g[0].send = S->hsend;
   g[0].recv = S->hrecv;
   g[0].count = (size_t)S->rmax * m->H;
@@ -250,9 +308,14 @@ Status sharded_select(wedlm_ctx* ctx, DecodeSession* S, EntropyArgs& A, int nin,
   g[1].recv = S->shdr + 4;
   g[1].count = 4;
   g[1].dtype = kCommInt32;
+  g[2].send = S->usend;
+  g[2].recv = S->urecv;
+  g[2].count = (size_t)S->rmax;
+  g[2].dtype = WEDLM_F32;
   int pc = prof_begin(ctx, st);
-  Status sg = comm_all_gather(c, g, 2, st);
-  prof_end(ctx, st, pc, WedlmProfiler::kComm, (double)n * (g[0].count * m->esz + 16), 0, 0);
+  Status sg = comm_all_gather(c, g, sample ? 3 : 2, st);
+  prof_end(ctx, st, pc, WedlmProfiler::kComm,
+           (double)n * (g[0].count * m->esz + 16 + (sample ? S->rmax * 4 : 0)), 0, 0);
   WEDLM_TRY(sg);
 
   WEDLM_TRY(model_lm_head(ctx, S->hrecv, m->H, rows, S->slogits, m->dt, st));
@@ -282,6 +345,57 @@ Status sharded_select(wedlm_ctx* ctx, DecodeSession* S, EntropyArgs& A, int nin,
     ph = prof_begin(ctx, st);
     WEDLM_TRY(run_entropy_combine(S->precv + (size_t)me * S->rmax * 4, n, A, ctx->ent, st, rows));
     prof_end(ctx, st, ph, WedlmProfiler::kEntropy, (double)n * A.rows * 16, 0, 1);
+  }
+  if (sample) {
+    // T > 0: the picked rows of every rank are drawn over the split vocabulary (every
+    // rank runs the same phases); the owners' argmax of those rows is replaced
+    ShardSampleArgs sa;
+    sa.logits = S->slogits;
+    sa.dtype = m->dt;
+    sa.V = m->vshard;
+    sa.ld = m->vshard;
+    sa.vocab_begin = comm_shard_begin(c, me);
+    sa.V_total = m->V;
+    sa.nranks = n;
+    sa.me = me;
+    sa.rmax = S->rmax;
+    sa.temperature = S->prm.temperature;
+    sa.top_p = S->prm.top_p;
+    sa.hdr = S->shdr + 4;
+    sa.u = S->urecv;
+    sa.nseq = A.nseq;
+    sa.seq_rows = A.seq_rows;
+    sa.selected = A.selected;
+    sa.n_selected = A.n_selected;
+    sa.state = S->sstate;
+    sa.xsend = S->xsend;
+    sa.xrecv = S->xrecv;
+    sa.tokens = A.argmax;
+    // profiled as alternating groups: each phase kernel (entropy class), then its gather
+    struct GatherCtx {
+      wedlm_ctx* ctx;
+      Comm* c;
+      int n, open;
+    } gc{ctx, c, n, prof_begin(ctx, st)};
+    ShardGather sgf;
+    sgf.user = &gc;
+    sgf.fn = [](void* user, const void* send, void* recv, size_t bytes, cudaStream_t s) {
+      GatherCtx* G = static_cast<GatherCtx*>(user);
+      prof_end(G->ctx, s, G->open, WedlmProfiler::kEntropy, 0, 0, 1);
+      GatherPiece p;
+      p.send = send;
+      p.recv = recv;
+      p.count = bytes / 4;
+      p.dtype = kCommInt32;
+      const int pg = prof_begin(G->ctx, s);
+      Status r = comm_all_gather(G->c, &p, 1, s);
+      prof_end(G->ctx, s, pg, WedlmProfiler::kComm, (double)G->n * bytes, 0, 0);
+      G->open = prof_begin(G->ctx, s);
+      return r;
+    };
+    Status ss = run_shard_sample(sa, sgf, st);
+    prof_end(ctx, st, gc.open, WedlmProfiler::kEntropy, 0, 0, 1);
+    WEDLM_TRY(ss);
   }
   const size_t nout = (size_t)3 * S->rows_cap + A.nseq;
   int* ho = S->h_out;
