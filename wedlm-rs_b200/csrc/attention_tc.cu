@@ -70,6 +70,9 @@ struct AtParams {
   float* part_ml;  // [parts][128][2]
   float scale_log2;
   int* err;
+  // device-built plans: the live item counts (work, combine); NULL = the launch's own
+  const int* n_work_dev;
+  const int* n_comb_dev;
 };
 
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
@@ -101,6 +104,8 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
                     const __grid_constant__ CUtensorMap tmV, const AtParams p) {
   pdl_trigger();
   pdl_wait();
+  // a device-built plan launches its upper bound of items
+  if (p.n_work_dev && (int)blockIdx.x >= *p.n_work_dev) return;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -412,6 +417,7 @@ __global__ void attention_combine_kernel(const CombineItem* items, int nitems, A
   const int wid = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (wid >= nitems * kQT) return;
+  if (p.n_comb_dev && wid >= *p.n_comb_dev * kQT) return;
   const CombineItem it = items[wid / kQT];
   const int qr = wid % kQT;
   const int S = p.seq_rows[it.b];
@@ -550,6 +556,144 @@ Status plan_attention_tc(const AttnArgs& a, const int* h_seq_rows, const int* h_
   return Status::ok();
 }
 
+// ---- the same plan built on the device -------------------------------------------------
+// For the decode loop that keeps its bookkeeping on the device (the window rows and cache
+// lengths of a step exist only there): one CTA computes exactly the items
+// plan_attention_tc computes from host copies of the same lengths, in the same order.
+struct AttnDevPlan {
+  int nseq, nkv, group, num_sms, max_work, max_comb;
+  const int* seq_rows;
+  const int* seq_cache_len;
+  AttnWork* work;
+  CombineItem* comb;
+  int* counts;  // [2]: work items, combine items
+  int* err;
+};
+
+__device__ __forceinline__ int last_le(const int* off, int n, int v) {
+  int lo = 0, hi = n - 1;  // the last index b in [0, n) with off[b] <= v
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (off[mid] <= v) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+__global__ void attention_plan_kernel(AttnDevPlan a) {
+  pdl_trigger();
+  pdl_wait();
+  extern __shared__ int sh_off[];  // [3][nseq + 1]: work, combine and part offsets
+  int* wo = sh_off;
+  int* co = wo + a.nseq + 1;
+  int* po = co + a.nseq + 1;
+  __shared__ long s_base;
+  __shared__ int s_nw, s_nc;
+  auto tiles_of = [&](int S) { return (S * a.group + kQT - 1) / kQT; };
+  auto splits_of = [&](long base, int S, int L) {
+    const int chunks = (L + S + kKC - 1) / kKC;
+    int splits = base > 0 ? (int)(a.num_sms / base) : 1;
+    return splits < 1 ? 1 : (splits > chunks ? chunks : splits);
+  };
+  if (threadIdx.x == 0) {
+    long base = 0;
+    for (int b = 0; b < a.nseq; ++b) base += (long)a.nkv * tiles_of(a.seq_rows[b]);
+    int nw = 0, nc = 0, np = 0;
+    for (int b = 0; b < a.nseq; ++b) {
+      wo[b] = nw;
+      co[b] = nc;
+      po[b] = np;
+      const int S = a.seq_rows[b];
+      if (S == 0) continue;
+      const int tiles = tiles_of(S), splits = splits_of(base, S, a.seq_cache_len[b]);
+      nw += a.nkv * tiles * splits;
+      if (splits > 1) {
+        nc += a.nkv * tiles;
+        np += a.nkv * tiles * splits;
+      }
+    }
+    wo[a.nseq] = nw;
+    co[a.nseq] = nc;
+    po[a.nseq] = np;
+    if (nw > a.max_work || nc > a.max_comb) {  // outside the launch bound: run nothing
+      nw = nc = 0;
+      if (a.err) atomicCAS(a.err, 0, kErrAtPlan);
+    }
+    s_base = base;
+    s_nw = nw;
+    s_nc = nc;
+    a.counts[0] = nw;
+    a.counts[1] = nc;
+  }
+  __syncthreads();
+  const long base = s_base;
+  for (int i = threadIdx.x; i < s_nw; i += blockDim.x) {
+    const int b = last_le(wo, a.nseq, i);
+    const int S = a.seq_rows[b], L = a.seq_cache_len[b];
+    const int tiles = tiles_of(S), splits = splits_of(base, S, L);
+    const int chunks = (L + S + kKC - 1) / kKC;
+    const int local = i - wo[b];
+    const int s2 = local % splits, gt = local / splits;
+    AttnWork w;
+    w.b = b;
+    w.g = gt / tiles;
+    w.t = gt % tiles;
+    w.c0 = (int)((long)chunks * s2 / splits);
+    w.c1 = (int)((long)chunks * (s2 + 1) / splits);
+    w.split = s2;
+    w.part = splits > 1 ? po[b] + local : -1;
+    a.work[i] = w;
+  }
+  for (int j = threadIdx.x; j < s_nc; j += blockDim.x) {
+    const int b = last_le(co, a.nseq, j);
+    const int S = a.seq_rows[b];
+    const int tiles = tiles_of(S), splits = splits_of(base, S, a.seq_cache_len[b]);
+    const int local = j - co[b];
+    a.comb[j] = CombineItem{b, local / tiles, local % tiles, po[b] + local * splits, splits};
+  }
+}
+
+long attention_ws_floats_device(int max_work, int max_comb) {
+  return (long)max_work * 8 + (long)max_comb * 6 + 4 + (long)max_work * kQT * (kD + 2) + 64;
+}
+
+Status plan_attention_tc_device(const AttnArgs& a, int num_sms, float* ws, long ws_floats,
+                                int max_work, int max_comb, int* counts, int* err,
+                                AttnPlan* plan, cudaStream_t st) {
+  WEDLM_CHECK_ARG(a.head_dim == kD, "tensor-core attention needs head_dim 128");
+  WEDLM_CHECK_ARG(a.page_size == 64, "tensor-core attention needs 64-token pages");
+  WEDLM_CHECK_ARG(kQT % a.group == 0, "query tile must hold whole GQA groups");
+  WEDLM_CHECK_ARG(a.nseq >= 1 && a.nseq <= 4000, "bad number of sequences");
+  WEDLM_CHECK_ARG(max_work >= 1 && max_comb >= 1 && counts, "bad plan bounds");
+  WEDLM_CHECK_ARG(attention_ws_floats_device(max_work, max_comb) <= ws_floats,
+                  "attention workspace too small");
+  AttnDevPlan d;
+  d.nseq = a.nseq;
+  d.nkv = a.nkv;
+  d.group = a.group;
+  d.num_sms = num_sms;
+  d.max_work = max_work;
+  d.max_comb = max_comb;
+  d.seq_rows = a.seq_rows;
+  d.seq_cache_len = a.seq_cache_len;
+  d.work = reinterpret_cast<AttnWork*>(ws);
+  d.comb = reinterpret_cast<CombineItem*>(ws + (long)max_work * 8);
+  d.counts = counts;
+  d.err = err;
+  const size_t smem = sizeof(int) * 3 * (a.nseq + 1);
+  WEDLM_CUDA_TRY(launch_pdl(attention_plan_kernel, dim3(1), dim3(512), smem, st, d));
+  plan->n_work = max_work;
+  plan->n_comb = max_comb;
+  plan->work = ws;
+  plan->comb = ws + (long)max_work * 8;
+  float* po = ws + (long)max_work * 8 + (long)max_comb * 6;
+  po = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(po) + 15) & ~uintptr_t(15));
+  plan->part_o = po;
+  plan->part_ml = po + (long)max_work * kQT * kD;
+  plan->n_work_dev = counts;
+  plan->n_comb_dev = counts + 1;
+  return Status::ok();
+}
+
 Status run_attention_tc(const AttnArgs& a, const AttnPlan& plan, int* err, cudaStream_t st) {
   if (plan.n_work == 0) return Status::ok();
   CUtensorMap mQ, mK, mV;
@@ -580,6 +724,8 @@ Status run_attention_tc(const AttnArgs& a, const AttnPlan& plan, int* err, cudaS
   p.part_ml = plan.part_ml;
   p.scale_log2 = kLog2e / sqrtf((float)kD);
   p.err = err;
+  p.n_work_dev = plan.n_work_dev;
+  p.n_comb_dev = plan.n_comb_dev;
   const size_t smem = 1024 + (2 + kStages * 4 + 2) * kBlk + 16 * 8 + 4096 * 4 + kKC * 4 + 4 * kQT * 4;
   int dev = 0;
   WEDLM_CUDA_TRY(cudaGetDevice(&dev));

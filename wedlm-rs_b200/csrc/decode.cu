@@ -30,6 +30,7 @@
 #include <cmath>
 
 #include "comm.h"
+#include "decode_loop.h"
 #include "entropy_select.cuh"
 #include "model.h"
 #include "sample.cuh"
@@ -92,8 +93,13 @@ struct DecodeSession {
   ShardSampleRow* sstate = nullptr;   // [nranks * rmax]
   void* xsend = nullptr;              // shard_sample_xbytes
   void* xrecv = nullptr;              // nranks * shard_sample_xbytes
+  // The device-resident loop (decode_loop.cu) when it runs this session; `runs` then
+  // mirrors its state only after sync_loop.
+  DeviceLoop* loop = nullptr;
+  bool loop_stale = false;
 
   ~DecodeSession() {
+    if (loop) loop_free(loop);
     cudaFree(block);
     cudaFree(shdr);
     cudaFree(sblock);
@@ -103,7 +109,32 @@ struct DecodeSession {
   }
 };
 
+// Copy the device loop's outputs, statistics and committed cache lengths into the
+// session's host state (and the model's cache lengths).
+Status sync_loop(wedlm_ctx* ctx, DecodeSession* S) {
+  if (!S->loop || !S->loop_stale) return Status::ok();
+  std::vector<LoopSeqResult> res;
+  WEDLM_TRY(loop_results(ctx, S->loop, &res));
+  ModelState* m = ctx->model;
+  for (size_t b = 0; b < res.size() && b < S->runs.size(); ++b) {
+    SeqRun& R = S->runs[b];
+    const LoopSeqResult& r = res[b];
+    R.out = r.out;
+    R.done = r.done;
+    R.st.steps = r.steps;
+    R.st.tokens_generated = r.tokens_generated;
+    R.st.avg_entropy = r.entropy_sum;
+    R.st.max_entropy = r.entropy_max;
+    R.st.high_entropy_count = r.high_entropy_count;
+    m->cache_len[R.slot] = r.cache_len;
+    m->pending_rows[R.slot] = 0;
+  }
+  S->loop_stale = false;
+  return Status::ok();
+}
+
 void session_free(wedlm_ctx* ctx) {
+  if (ctx->session) sync_loop(ctx, ctx->session);  // the cache lengths of its slots
   delete ctx->session;
   ctx->session = nullptr;
 }
@@ -254,6 +285,18 @@ Status session_begin(wedlm_ctx* ctx, const std::vector<int>& slots, const int32_
   WEDLM_CUDA_TRY(cudaMemcpyAsync(S->running, r0.data(), B * 4, cudaMemcpyHostToDevice, st));
   if (ctx->comm) WEDLM_TRY(sharded_begin(ctx, S, st));
   WEDLM_CUDA_TRY(cudaStreamSynchronize(st));
+  if (device_loop_eligible(ctx, B, window, n_prompt, max_new)) {
+    LoopInit li;
+    li.W = window;
+    li.max_new = max_new;
+    li.n_prompt = n_prompt;
+    li.slots = slots;
+    li.prm = prm;
+    li.logits = S->logits;
+    li.running = S->running;
+    li.st = st ? st : m->stream;  // a graph cannot be captured on the legacy stream
+    WEDLM_TRY(loop_create(ctx, li, &S->loop));
+  }
   return Status::ok();
 }
 
@@ -682,9 +725,18 @@ int wedlm_decode_step(wedlm_ctx* ctx, int n_steps, int32_t* n_live) {
   if (int rc = wedlm::guard(ctx)) return rc;
   if (!ctx->session) return ctx->fail(Status::err(WEDLM_ERR_STATE, "no decode session"));
   int live = 1;
-  for (int i = 0; i < n_steps && live > 0; ++i) {
-    Status s = wedlm::session_step(ctx, &live);
+  wedlm::DecodeSession* S = ctx->session;
+  if (S->loop) {
+    int64_t steps = -1;
+    S->loop_stale = true;
+    Status s = wedlm::loop_run(ctx, S->loop, n_steps, &live, &steps);
     if (!s.good()) return ctx->fail(s);
+    if (steps >= 0) S->steps = steps;
+  } else {
+    for (int i = 0; i < n_steps && live > 0; ++i) {
+      Status s = wedlm::session_step(ctx, &live);
+      if (!s.good()) return ctx->fail(s);
+    }
   }
   if (n_live) *n_live = live;
   return WEDLM_OK;
@@ -696,6 +748,8 @@ int wedlm_decode_result(wedlm_ctx* ctx, int b, int32_t* out_ids, int32_t* n_out,
   if (!ctx->session) return ctx->fail(Status::err(WEDLM_ERR_STATE, "no decode session"));
   if (b < 0 || b >= (int)ctx->session->runs.size())
     return ctx->fail(Status::err(WEDLM_ERR_INVALID_ARG, "bad sequence index"));
+  Status sl = wedlm::sync_loop(ctx, ctx->session);
+  if (!sl.good()) return ctx->fail(sl);
   const wedlm::SeqRun& R = ctx->session->runs[b];
   if (out_ids)
     for (size_t i = 0; i < R.out.size(); ++i) out_ids[i] = R.out[i];
@@ -707,9 +761,12 @@ int wedlm_decode_result(wedlm_ctx* ctx, int b, int32_t* out_ids, int32_t* n_out,
 int wedlm_decode_io_bytes(const wedlm_ctx* ctx, int64_t* steps, int64_t* h2d_bytes,
                           int64_t* d2h_bytes) {
   if (!ctx || !ctx->session) return WEDLM_ERR_STATE;
-  if (steps) *steps = ctx->session->steps;
-  if (h2d_bytes) *h2d_bytes = ctx->session->h2d_bytes;
-  if (d2h_bytes) *d2h_bytes = ctx->session->d2h_bytes;
+  const wedlm::DecodeSession* S = ctx->session;
+  int64_t lh = 0, ld = 0;
+  if (S->loop) wedlm::loop_io_bytes(S->loop, &lh, &ld);
+  if (steps) *steps = S->steps;
+  if (h2d_bytes) *h2d_bytes = S->h2d_bytes + lh;
+  if (d2h_bytes) *d2h_bytes = S->d2h_bytes + ld;
   return WEDLM_OK;
 }
 

@@ -401,6 +401,9 @@ entropy_select_kernel(const T* __restrict__ logits, int V, long ld, int splits, 
     for (int b = threadIdx.x; b < nseq; b += kThreads)
       if (seq_rows[b + 1] == seq_rows[b]) n_selected[b] = 0;
   }
+  // rows past the last sequence's end: a launch sized for more rows than this step holds
+  // (the device-resident decode loop launches its row capacity)
+  if (row >= seq_rows[nseq]) return;
   const float a = invT * kLog2e;
 
   Acc st;

@@ -67,16 +67,27 @@ Status run_attention_f32(const AttnArgs& a, cudaStream_t st);
 // built once per forward from host copies of the per-sequence window and cache lengths
 // and uploaded into the workspace `ws`; run_attention_tc is then called per layer.
 struct AttnPlan {
-  int n_work = 0, n_comb = 0;
+  int n_work = 0, n_comb = 0;  // launch sizes (device-built plans: upper bounds)
   const float* work = nullptr;
   const float* comb = nullptr;
   float* part_o = nullptr;
   float* part_ml = nullptr;
+  const int* n_work_dev = nullptr;  // device-built plans: the item counts of the step
+  const int* n_comb_dev = nullptr;
 };
 long attention_ws_floats(const AttnArgs& a);
 Status plan_attention_tc(const AttnArgs& a, const int* h_seq_rows, const int* h_cache_len,
                          int num_sms, float* ws, long ws_floats, void* h_staging,
                          size_t staging_bytes, AttnPlan* plan, cudaStream_t st);
+// The same plan built on the device from a.seq_rows / a.seq_cache_len (device arrays of
+// the step), for at most max_work work items and max_comb combine items: a sequence-
+// independent upper bound is max(num_sms, sum over sequences of nkv * ceil(S * group /
+// 128)).  counts (device int[2]) receives the item counts; err records a plan that did
+// not fit the bounds (nothing runs then).  Workspace: attention_ws_floats_device floats.
+long attention_ws_floats_device(int max_work, int max_comb);
+Status plan_attention_tc_device(const AttnArgs& a, int num_sms, float* ws, long ws_floats,
+                                int max_work, int max_comb, int* counts, int* err,
+                                AttnPlan* plan, cudaStream_t st);
 Status run_attention_tc(const AttnArgs& a, const AttnPlan& plan, int* err, cudaStream_t st);
 
 }  // namespace wedlm

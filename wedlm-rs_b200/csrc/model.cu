@@ -435,62 +435,21 @@ void model_destroy(wedlm_ctx* ctx) {
 }
 
 // ---- forward --------------------------------------------------------------------------
-Status model_forward(wedlm_ctx* ctx, const std::vector<SeqSlice>& seqs, const int* tokens,
-                     const int* positions, const int* rank, void* logits, int logits_dtype,
-                     int* n_logit_rows, cudaStream_t st, void* hidden_out) {
-  ModelState* m = ctx->model;
-  const int B = (int)seqs.size();
-  WEDLM_CHECK_ARG(B >= 1 && B <= m->max_seqs, "bad number of sequences");
-  int R = 0, RL = 0;
-  for (const SeqSlice& s : seqs) {
-    WEDLM_CHECK_ARG(s.slot >= 0 && s.slot < m->max_seqs, "bad cache slot");
-    WEDLM_CHECK_ARG(s.rows >= 0 && s.logit_begin >= 0 && s.logit_begin <= s.rows, "bad window");
-    WEDLM_CHECK_ARG(m->cache_len[s.slot] + s.rows <= m->max_ctx,
-                    "window does not fit the KV cache (max_ctx)");
-    R += s.rows;
-    RL += s.rows - s.logit_begin;
-  }
-  WEDLM_CHECK_ARG(R <= m->max_rows, "more window rows than the context was created for");
-  if (n_logit_rows) *n_logit_rows = RL;
-  for (int i = 0; i < R; ++i) {
-    WEDLM_CHECK_ARG(tokens[i] >= 0 && tokens[i] < m->V, "token id out of range");
-    WEDLM_CHECK_ARG(positions[i] >= 0 && positions[i] < m->cfg.max_position_embeddings,
-                    "position out of range of the RoPE table");
-  }
-  WEDLM_CHECK_ARG(logits_dtype == m->dt || logits_dtype == WEDLM_F32 || !logits,
-                  "logits dtype must be the model dtype or F32");
-  if (R == 0) return Status::ok();
+namespace {
 
-  // ---- metadata (one upload) ----
-  int* hm = m->h_meta;
-  const int o_tok = 0, o_pos = R, o_rank = 2 * R, o_rslot = 3 * R, o_dst = 4 * R, o_rb = 5 * R,
-            o_lsrc = 6 * R, o_s0 = 7 * R, o_sr = o_s0 + B, o_sl = o_sr + B, o_ss = o_sl + B;
-  const int total = o_ss + B;
-  WEDLM_CHECK_ARG((size_t)total <= m->meta_ints, "metadata buffer too small");
-  // the pinned staging buffer is reused by the next forward: wait for its last upload
-  WEDLM_CUDA_TRY(cudaStreamSynchronize(st));
-  int r = 0, rl = 0;
-  std::vector<int> h_rows(B), h_len(B);
-  for (int b = 0; b < B; ++b) {
-    const SeqSlice& s = seqs[b];
-    hm[o_s0 + b] = r;
-    hm[o_sr + b] = s.rows;
-    hm[o_sl + b] = m->cache_len[s.slot];
-    hm[o_ss + b] = s.slot;
-    h_rows[b] = s.rows;
-    h_len[b] = m->cache_len[s.slot];
-    for (int j = 0; j < s.rows; ++j, ++r) {
-      hm[o_tok + r] = tokens[r];
-      hm[o_pos + r] = positions[r];
-      hm[o_rank + r] = rank ? rank[r] : j;
-      hm[o_rslot + r] = s.slot;
-      hm[o_dst + r] = m->cache_len[s.slot] + j;
-      hm[o_rb + r] = b;
-      if (j >= s.logit_begin) hm[o_lsrc + rl++] = r;
-    }
-  }
-  WEDLM_CUDA_TRY(cudaMemcpyAsync(m->d_meta, hm, (size_t)total * 4, cudaMemcpyHostToDevice, st));
-  const int* d = m->d_meta;
+// The forward after its metadata is on the device (d, layout ml): embedding, the layers,
+// the final norm, the logit-row gather and the LM head.  h_rows / h_len: host copies of
+// the window rows and cache lengths (device mode: the window capacity and upper bounds of
+// the lengths, used for the profiler's byte counts; the attention plan is then built on
+// the device from the step's own lengths).
+Status forward_body(wedlm_ctx* ctx, int B, int R, int RL, const int* d, const MetaLayout& ml,
+                    const int* h_rows_p, const int* h_len_p, const DeviceForward* dev,
+                    void* logits, int logits_dtype, cudaStream_t st, void* hidden_out) {
+  ModelState* m = ctx->model;
+  const int o_tok = ml.tok, o_pos = ml.pos, o_rank = ml.rank, o_rslot = ml.rslot, o_dst = ml.dst,
+            o_rb = ml.rb, o_lsrc = ml.lsrc, o_s0 = ml.s0, o_sr = ml.sr, o_sl = ml.sl, o_ss = ml.ss;
+  (void)o_ss;
+  std::vector<int> h_rows(h_rows_p, h_rows_p + B), h_len(h_len_p, h_len_p + B);
 
   const long H = m->H;
   const int es = m->esz;
@@ -533,7 +492,13 @@ Status model_forward(wedlm_ctx* ctx, const std::vector<SeqSlice>& seqs, const in
   aa.max_kv = maxkv;
   const bool tc = m->dt == WEDLM_BF16;
   AttnPlan plan;
-  if (tc) {
+  if (tc && dev) {
+    const int ph = prof_begin(ctx, st);
+    Status sp = plan_attention_tc_device(aa, ctx->num_sms, dev->attn_ws, dev->attn_ws_floats,
+                                         dev->max_work, dev->max_comb, dev->counts, err, &plan, st);
+    prof_end(ctx, st, ph, WedlmProfiler::kOther, 0, 0, 1);
+    WEDLM_TRY(sp);
+  } else if (tc) {
     WEDLM_CHECK_ARG(m->attn_ws != nullptr, "tensor-core attention needs head_dim 128");
     WEDLM_TRY(plan_attention_tc(aa, h_rows.data(), h_len.data(), ctx->num_sms, m->attn_ws,
                                 m->attn_ws_floats, m->h_attn_staging, m->attn_staging_bytes, &plan,
@@ -773,7 +738,6 @@ Status model_forward(wedlm_ctx* ctx, const std::vector<SeqSlice>& seqs, const in
                      nullptr));
     }
   }
-  for (int b = 0; b < B; ++b) m->pending_rows[seqs[b].slot] = seqs[b].rows;
   if ((!logits && !hidden_out) || RL == 0) return Status::ok();
 
   if (!tc) {
@@ -783,7 +747,8 @@ Status model_forward(wedlm_ctx* ctx, const std::vector<SeqSlice>& seqs, const in
     WEDLM_TRY(sn);
   }
   const void* xl = m->xn;
-  if (RL != R || hidden_out) {
+  // (device mode: the mask rows in selection order, then padding rows, always gathered)
+  if (RL != R || hidden_out || dev) {
     void* dst = hidden_out ? hidden_out : m->xl;
     ctx->launches += 1;
     if (m->dt == WEDLM_BF16)
@@ -799,6 +764,85 @@ Status model_forward(wedlm_ctx* ctx, const std::vector<SeqSlice>& seqs, const in
   if (hidden_out) return Status::ok();
   (void)es;
   return model_lm_head(ctx, xl, H, RL, logits, logits_dtype, st);
+}
+
+}  // namespace
+
+Status model_forward(wedlm_ctx* ctx, const std::vector<SeqSlice>& seqs, const int* tokens,
+                     const int* positions, const int* rank, void* logits, int logits_dtype,
+                     int* n_logit_rows, cudaStream_t st, void* hidden_out) {
+  ModelState* m = ctx->model;
+  const int B = (int)seqs.size();
+  WEDLM_CHECK_ARG(B >= 1 && B <= m->max_seqs, "bad number of sequences");
+  int R = 0, RL = 0;
+  for (const SeqSlice& s : seqs) {
+    WEDLM_CHECK_ARG(s.slot >= 0 && s.slot < m->max_seqs, "bad cache slot");
+    WEDLM_CHECK_ARG(s.rows >= 0 && s.logit_begin >= 0 && s.logit_begin <= s.rows, "bad window");
+    WEDLM_CHECK_ARG(m->cache_len[s.slot] + s.rows <= m->max_ctx,
+                    "window does not fit the KV cache (max_ctx)");
+    R += s.rows;
+    RL += s.rows - s.logit_begin;
+  }
+  WEDLM_CHECK_ARG(R <= m->max_rows, "more window rows than the context was created for");
+  if (n_logit_rows) *n_logit_rows = RL;
+  for (int i = 0; i < R; ++i) {
+    WEDLM_CHECK_ARG(tokens[i] >= 0 && tokens[i] < m->V, "token id out of range");
+    WEDLM_CHECK_ARG(positions[i] >= 0 && positions[i] < m->cfg.max_position_embeddings,
+                    "position out of range of the RoPE table");
+  }
+  WEDLM_CHECK_ARG(logits_dtype == m->dt || logits_dtype == WEDLM_F32 || !logits,
+                  "logits dtype must be the model dtype or F32");
+  if (R == 0) return Status::ok();
+
+  // ---- metadata (one upload) ----
+  int* hm = m->h_meta;
+  const MetaLayout ml(R, B);
+  const int o_tok = ml.tok, o_pos = ml.pos, o_rank = ml.rank, o_rslot = ml.rslot, o_dst = ml.dst,
+            o_rb = ml.rb, o_lsrc = ml.lsrc, o_s0 = ml.s0, o_sr = ml.sr, o_sl = ml.sl, o_ss = ml.ss;
+  const int total = ml.total;
+  WEDLM_CHECK_ARG((size_t)total <= m->meta_ints, "metadata buffer too small");
+  // the pinned staging buffer is reused by the next forward: wait for its last upload
+  WEDLM_CUDA_TRY(cudaStreamSynchronize(st));
+  int r = 0, rl = 0;
+  std::vector<int> h_rows(B), h_len(B);
+  for (int b = 0; b < B; ++b) {
+    const SeqSlice& s = seqs[b];
+    hm[o_s0 + b] = r;
+    hm[o_sr + b] = s.rows;
+    hm[o_sl + b] = m->cache_len[s.slot];
+    hm[o_ss + b] = s.slot;
+    h_rows[b] = s.rows;
+    h_len[b] = m->cache_len[s.slot];
+    for (int j = 0; j < s.rows; ++j, ++r) {
+      hm[o_tok + r] = tokens[r];
+      hm[o_pos + r] = positions[r];
+      hm[o_rank + r] = rank ? rank[r] : j;
+      hm[o_rslot + r] = s.slot;
+      hm[o_dst + r] = m->cache_len[s.slot] + j;
+      hm[o_rb + r] = b;
+      if (j >= s.logit_begin) hm[o_lsrc + rl++] = r;
+    }
+  }
+  WEDLM_CUDA_TRY(cudaMemcpyAsync(m->d_meta, hm, (size_t)total * 4, cudaMemcpyHostToDevice, st));
+  WEDLM_TRY(forward_body(ctx, B, R, RL, m->d_meta, ml, h_rows.data(), h_len.data(), nullptr, logits,
+                         logits_dtype, st, hidden_out));
+  for (int b = 0; b < B; ++b) m->pending_rows[seqs[b].slot] = seqs[b].rows;
+  return Status::ok();
+}
+
+Status model_forward_device(wedlm_ctx* ctx, const DeviceForward& df, void* logits,
+                            int logits_dtype, cudaStream_t st) {
+  ModelState* m = ctx->model;
+  const int B = df.B, R = df.B * df.W;
+  WEDLM_CHECK_ARG(B >= 1 && B <= m->max_seqs && df.W >= 1, "bad device forward shape");
+  WEDLM_CHECK_ARG(R <= m->max_rows, "more window rows than the context was created for");
+  WEDLM_CHECK_ARG((size_t)MetaLayout(R, B).total <= m->meta_ints, "metadata buffer too small");
+  WEDLM_CHECK_ARG(logits_dtype == m->dt || logits_dtype == WEDLM_F32,
+                  "logits dtype must be the model dtype or F32");
+  std::vector<int> h_rows(B, df.W);
+  std::vector<int> h_len(df.len_bound, df.len_bound + B);
+  return forward_body(ctx, B, R, R, m->d_meta, MetaLayout(R, B), h_rows.data(), h_len.data(), &df,
+                      logits, logits_dtype, st, nullptr);
 }
 
 Status model_lm_head(wedlm_ctx* ctx, const void* x, long ldx, int M, void* logits,

@@ -30,6 +30,31 @@ struct SeqSlice {
   int logit_begin = 0;
 };
 
+// Layout of the per-forward metadata (ints, device): R rows of B sequences.
+struct MetaLayout {
+  int tok, pos, rank, rslot, dst, rb, lsrc;  // [R] each: token, position, mask rank, cache
+                                              // slot, cache row, sequence, logit-row source
+  int s0, sr, sl, ss;                         // [B] each: first row, attention rows (window
+                                              // length), committed cache length, cache slot
+  int total;
+  MetaLayout(int R, int B)
+      : tok(0), pos(R), rank(2 * R), rslot(3 * R), dst(4 * R), rb(5 * R), lsrc(6 * R), s0(7 * R),
+        sr(7 * R + B), sl(7 * R + 2 * B), ss(7 * R + 3 * B), total(7 * R + 4 * B) {}
+};
+
+// A forward whose metadata a device kernel wrote into the model's metadata buffer (the
+// device-resident decode loop): B sequences of W rows each (row b * W + j), every row
+// projected; the logit rows (lsrc) are the step's mask rows followed by padding rows.
+// The attention plan is built on the device (plan_attention_tc_device) into attn_ws.
+struct DeviceForward {
+  int B = 0, W = 0;
+  const int* len_bound = nullptr;  // host [B]: upper bounds of the cache lengths (profiler)
+  float* attn_ws = nullptr;
+  long attn_ws_floats = 0;
+  int max_work = 0, max_comb = 0;
+  int* counts = nullptr;           // device int[2]
+};
+
 struct ModelState {
   wedlm_config cfg{};
   int dt = WEDLM_BF16, esz = 2;
@@ -88,6 +113,12 @@ void model_destroy(wedlm_ctx* ctx);
 Status model_forward(wedlm_ctx* ctx, const std::vector<SeqSlice>& seqs, const int* tokens,
                      const int* positions, const int* rank, void* logits, int logits_dtype,
                      int* n_logit_rows, cudaStream_t st, void* hidden_out = nullptr);
+
+// The forward of a DeviceForward step: logits [B * W, vshard] (rows in lsrc order).  Every
+// launch's shape is fixed by (B, W): the step can be captured in a CUDA graph once the
+// scratch buffers have grown to it.
+Status model_forward_device(wedlm_ctx* ctx, const DeviceForward& df, void* logits,
+                            int logits_dtype, cudaStream_t st);
 
 // The LM head alone (this context's vocabulary shard) over M final-normed hidden rows
 // x ([M, ldx], model dtype, device): logits [M, vshard] of dtype logits_dtype.

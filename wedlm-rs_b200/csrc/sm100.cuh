@@ -35,6 +35,7 @@ enum ErrCode : int {
   kErrAtSoftS = 23,
   kErrAtSoftO = 24,
   kErrAtSoftOLast = 25,
+  kErrAtPlan = 26,  // a device-built attention plan exceeded its launch bounds (no wait)
   // fused layer tail: 32 + wait site; grid-wide dependency counter k: 48 + k
   kErrFuEmptyW = 32,
   kErrFuEmptyX = 33,
@@ -46,6 +47,8 @@ enum ErrCode : int {
   kErrFuDrainX = 39,
   kErrFuStep = 40,
   kErrFuGrid = 48,
+  // the device-resident decode loop: a step's rows exceeded the buffers (no wait)
+  kErrLoopRows = 96,
 };
 
 __device__ __forceinline__ uint64_t global_ns() {
