@@ -604,7 +604,8 @@ Status session_step(wedlm_ctx* ctx, int* live_after) {
     A.logits = S->logits;
     A.V = m->vshard;
     A.ld = m->vshard;
-    EntropyPlan ep = plan_entropy(rr, m->vshard, m->dt, ctx->num_sms);
+    A.plan_rows = S->rows_cap;  // the device loop's split: the same merge order per row
+    EntropyPlan ep = plan_entropy(S->rows_cap, m->vshard, m->dt, ctx->num_sms);
     WEDLM_TRY(ensure_entropy_scratch(ctx, rr, nb, (long)rr * ep.splits * 4));
     const int ph = prof_begin(ctx, st);
     WEDLM_TRY(run_entropy_select(A, ctx->ent, ctx->num_sms, st));

@@ -26,7 +26,7 @@ namespace wedlm {
 namespace {
 
 constexpr float kSoftThreshold = 8.0f;  // ENTROPY_SOFT_THRESHOLD, wedlm.rs:29
-constexpr int kLoopThreads = 1024;
+constexpr int kLoopThreads = 512;
 
 struct LoopDev {
   int B = 0, W = 0, max_new = 0, mask = 0, eos = 0, cap = 0;
@@ -110,6 +110,7 @@ __global__ void __launch_bounds__(kLoopThreads) loop_prep_kernel(LoopDev a) {
         a.meta[ml.rslot + r] = sl;
         a.meta[ml.dst + r] = cl + ri;
         a.meta[ml.rb + r] = b;
+        a.meta[ml.act + r] = in ? 1 : 0;
       }
     }
     if (lane == 0) {
@@ -335,6 +336,7 @@ Status enqueue_step(wedlm_ctx* ctx, DeviceLoop* L) {
   A.argmax = L->tokens;
   A.selected = L->selected;
   A.n_selected = L->n_selected;
+  A.plan_rows = R;
   ph = prof_begin(ctx, st);
   Status se = run_entropy_select(A, ctx->ent, ctx->num_sms, st);
   prof_end(ctx, st, ph, WedlmProfiler::kEntropy, (double)R * m->vshard * m->esz, 0, 1);
@@ -470,7 +472,7 @@ Status loop_create(wedlm_ctx* ctx, const LoopInit& in, DeviceLoop** out) {
   d.n_selected = L->n_selected;
   d.meta = m->d_meta;
   d.ml = MetaLayout(R, B);
-  WEDLM_CHECK_ARG((size_t)d.ml.total <= m->meta_ints, "metadata buffer too small");
+  WEDLM_CHECK_ARG((size_t)d.ml.total_dev <= m->meta_ints, "metadata buffer too small");
 
   WEDLM_CUDA_TRY(cudaMalloc(&L->floats, sizeof(float) * ((long)2 * B + R + 8)));
   d.ent_sum = L->floats;
@@ -507,8 +509,10 @@ Status loop_create(wedlm_ctx* ctx, const LoopInit& in, DeviceLoop** out) {
   df.len_bound = L->len_bound.data();
   if (m->dt == WEDLM_BF16) {
     const long tiles = (long)B * m->nkv * ((W * m->group + 127) / 128);
+    // work items <= max(SMs, tiles) (splits = SMs / tiles when that is above 1); combine
+    // items: at most one per tile
     L->max_work = (int)std::max<long>(ctx->num_sms, tiles);
-    L->max_comb = L->max_work;
+    L->max_comb = (int)std::max<long>(1, tiles);
     const long wsf = attention_ws_floats_device(L->max_work, L->max_comb);
     WEDLM_CUDA_TRY(cudaMalloc(&L->attn_ws, wsf * sizeof(float)));
     df.attn_ws = L->attn_ws;

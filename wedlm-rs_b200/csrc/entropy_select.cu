@@ -584,7 +584,7 @@ Status run_entropy_select(const EntropyArgs& A, const EntropyScratch& W, int num
   }
   WEDLM_CHECK_ARG(A.seq_rows && A.mask_pos && A.caps && A.selected,
                   "seq_rows, mask_pos, caps, selected and n_selected are required");
-  EntropyPlan p = plan_entropy(A.rows, A.V, A.dtype, num_sms);
+  EntropyPlan p = plan_entropy(A.plan_rows > 0 ? A.plan_rows : A.rows, A.V, A.dtype, num_sms);
   WEDLM_CHECK_ARG((long)A.rows * p.splits * 4 <= W.partial_capacity, "entropy scratch too small");
   WEDLM_CHECK_ARG(A.rows <= W.row_capacity && A.nseq <= W.seq_capacity, "entropy scratch too small");
   const bool vec = ((uintptr_t)A.logits % 16 == 0) && ((A.ld * dtype_size(A.dtype)) % 16 == 0);

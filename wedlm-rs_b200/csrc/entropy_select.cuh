@@ -25,6 +25,10 @@ struct EntropyArgs {
   float* maxprob = nullptr;
   int* selected = nullptr;
   int* n_selected = nullptr;
+  // Rows the vocabulary split is planned for (0: rows).  The decode loops plan for their
+  // row capacity, so that a row's statistics are merged in the same order whatever the
+  // step's row count (the host loop's mask rows, the device loop's padded rows).
+  int plan_rows = 0;
 };
 
 // Scratch (global memory) the kernels need besides their inputs and outputs.

@@ -661,7 +661,11 @@ GemmPlan plan_gemm_tc(int M, int N, int K, bool dual, int num_sms, int force_nb)
   else ks = 4;  // largest stage that still leaves two stages in the budget (see below)
   while (ks > 1 && (kb64 % ks != 0)) ks >>= 1;
   if (ks < 1) ks = 1;
-  while (ks > 1 && 2u * ks * (kATileBytes * na * nb + g.tok_tile * kBK * 2) > 192u * 1024u)
+  // The k-partition follows the token-tile class (up to 128 or up to 256 rows), not the
+  // exact row count: a row's split-K sums then come out the same at any row count of its
+  // class (a decode window of w rows, or the same window padded to the loop's capacity).
+  const int tt_class = g.tok_tile <= 128 ? 128 : 256;
+  while (ks > 1 && 2u * ks * (kATileBytes * na * nb + tt_class * kBK * 2) > 192u * 1024u)
     ks >>= 1;
   g.ks = ks;
   g.kb64 = kb64;

@@ -23,10 +23,11 @@ __device__ __forceinline__ T rnd(float v) {
 // ---- embedding -------------------------------------------------------------------
 template <typename T>
 __global__ void embed_kernel(const T* __restrict__ table, const int* __restrict__ ids, int H,
-                             T* __restrict__ out, int vocab, int* err) {
+                             T* __restrict__ out, int vocab, int* err, const int* act) {
   pdl_trigger();
   pdl_wait();
   const int r = blockIdx.x;
+  if (act && !act[r]) return;  // a padding row of the device loop
   int id = ids[r];
   if (id < 0 || id >= vocab) {
     if (threadIdx.x == 0) atomicCAS(err, 0, 100);
@@ -82,6 +83,7 @@ __global__ void rope_kv_kernel(RopeKvArgs a, PartialSet ps_val) {
   const int lane = threadIdx.x & 31;
   const int heads = a.nh + 2 * a.nkv;
   if (gw >= a.rows * heads) return;
+  if (a.row_active && !a.row_active[gw / heads]) return;  // a padding row of the device loop
   rope_kv_item<T, E>(a, a.qkv_partials != nullptr ? &ps_val : nullptr, gw, lane);
 }
 
@@ -133,11 +135,12 @@ __global__ void attention_f32_kernel(AttnArgs a) {
 // ---- residual add (from split-K partials) fused with the next RMSNorm ----------------
 __global__ void __launch_bounds__(512)
 resid_norm_kernel(__nv_bfloat16* h, PartialSet ps, int has_ps, const float* __restrict__ w,
-                  int H, float eps, __nv_bfloat16* xn) {
+                  int H, float eps, __nv_bfloat16* xn, const int* act) {
   pdl_trigger();
   pdl_wait();
   extern __shared__ float srow[];
   const int r = blockIdx.x;
+  if (act && !act[r]) return;  // a padding row of the device loop
   __nv_bfloat16* hr = h + (long)r * H;
   float ss = 0.f;
   // two float4 groups per iteration, every load of both issued before the arithmetic
@@ -203,44 +206,48 @@ resid_norm_kernel(__nv_bfloat16* h, PartialSet ps, int has_ps, const float* __re
 }
 
 // ---- SwiGLU from the gate/up partials (swiglu_range, layer_ops_dev.cuh) -------------
-__global__ void swiglu_kernel(PartialSet ps, int rows, int I, __nv_bfloat16* act) {
+__global__ void swiglu_kernel(PartialSet ps, int rows, int I, __nv_bfloat16* act,
+                              const int* row_active) {
   pdl_trigger();
   pdl_wait();
   swiglu_range(ps, rows, I, act, blockIdx.x * (long)blockDim.x + threadIdx.x,
-               (long)gridDim.x * blockDim.x);
+               (long)gridDim.x * blockDim.x, row_active);
 }
 
 }  // namespace
 
 Status run_resid_norm(void* h, const PartialSet* ps, const float* w, int rows, int H, float eps,
-                      void* xn, cudaStream_t st) {
+                      void* xn, cudaStream_t st, const int* row_active) {
   if (rows == 0) return Status::ok();
   WEDLM_CHECK_ARG(H % 4 == 0, "hidden size must be a multiple of 4");
   const PartialSet p = ps ? *ps : PartialSet();
   WEDLM_CUDA_TRY(launch_pdl(resid_norm_kernel, dim3(rows), dim3(512), (size_t)H * sizeof(float), st,
-                            (__nv_bfloat16*)h, p, ps ? 1 : 0, w, H, eps, (__nv_bfloat16*)xn));
+                            (__nv_bfloat16*)h, p, ps ? 1 : 0, w, H, eps, (__nv_bfloat16*)xn,
+                            row_active));
   return Status::ok();
 }
 
-Status run_swiglu(const PartialSet& ps, int rows, int I, void* act, cudaStream_t st) {
+Status run_swiglu(const PartialSet& ps, int rows, int I, void* act, cudaStream_t st,
+                  const int* row_active) {
   if (rows == 0) return Status::ok();
   WEDLM_CHECK_ARG(I % 4 == 0, "intermediate size must be a multiple of 4");
   const long n4 = (long)rows * I / 4;
   const unsigned grid = (unsigned)std::min<long>((n4 + 255) / 256, 148L * 16);
   WEDLM_CUDA_TRY(launch_pdl(swiglu_kernel, dim3(grid), dim3(256), 0, st, ps, rows, I,
-                            (__nv_bfloat16*)act));
+                            (__nv_bfloat16*)act, row_active));
   return Status::ok();
 }
 
 Status run_embed(const void* table, int dtype, const int* ids, int rows, int H, int vocab,
-                 void* out, int* err, cudaStream_t st) {
+                 void* out, int* err, cudaStream_t st, const int* row_active) {
   if (rows == 0) return Status::ok();
   if (dtype == WEDLM_BF16)
     WEDLM_CUDA_TRY(launch_pdl(embed_kernel<__nv_bfloat16>, dim3(rows), dim3(128), 0, st,
-                              (const __nv_bfloat16*)table, ids, H, (__nv_bfloat16*)out, vocab, err));
+                              (const __nv_bfloat16*)table, ids, H, (__nv_bfloat16*)out, vocab, err,
+                              row_active));
   else
     WEDLM_CUDA_TRY(launch_pdl(embed_kernel<float>, dim3(rows), dim3(128), 0, st,
-                              (const float*)table, ids, H, (float*)out, vocab, err));
+                              (const float*)table, ids, H, (float*)out, vocab, err, row_active));
   return Status::ok();
 }
 

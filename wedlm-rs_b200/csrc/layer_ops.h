@@ -33,6 +33,8 @@ struct RopeKvArgs : KvGeom {
   void* q_out = nullptr;           // group-major [nkv][rows * group][d]
   // bf16 models: the QKV projection as split-K partials (summed and rounded here)
   const PartialSet* qkv_partials = nullptr;
+  // [rows] or NULL: rows with 0 are skipped (the device loop's padding rows)
+  const int* row_active = nullptr;
 };
 
 struct AttnArgs : KvGeom {
@@ -49,8 +51,10 @@ struct AttnArgs : KvGeom {
   int nseq = 0, max_kv = 0;            // max_kv = max_b (L_b + S_b)
 };
 
+// row_active ([rows] or NULL, also below): rows with 0 are skipped (the device loop's
+// padding rows keep whatever they held).
 Status run_embed(const void* table, int dtype, const int* ids, int rows, int H, int vocab,
-                 void* out, int* err, cudaStream_t st);
+                 void* out, int* err, cudaStream_t st, const int* row_active = nullptr);
 Status run_rmsnorm(const void* x, long ldx, const float* w, int rows, int H, float eps, int dtype,
                    void* out, long ldo, cudaStream_t st);
 Status run_rope_kv(const RopeKvArgs& a, int dtype, cudaStream_t st);
@@ -58,9 +62,10 @@ Status run_rope_kv(const RopeKvArgs& a, int dtype, cudaStream_t st);
 // xn = RMSNorm(h) * w (rounded to bf16): the residual add of layer.rs:72,78 fused with
 // the next RMSNorm (attention.rs:35-50).
 Status run_resid_norm(void* h, const PartialSet* ps, const float* w, int rows, int H, float eps,
-                      void* xn, cudaStream_t st);
+                      void* xn, cudaStream_t st, const int* row_active = nullptr);
 // bf16: act = bf16(silu(bf16(gate)) * bf16(up)) from the gate/up partials (mlp.rs:40-43).
-Status run_swiglu(const PartialSet& ps, int rows, int I, void* act, cudaStream_t st);
+Status run_swiglu(const PartialSet& ps, int rows, int I, void* act, cudaStream_t st,
+                  const int* row_active = nullptr);
 Status run_attention_f32(const AttnArgs& a, cudaStream_t st);
 
 // bf16 block attention on the tensor cores.  The plan (work items, split-KV layout) is

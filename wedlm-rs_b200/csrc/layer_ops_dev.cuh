@@ -115,11 +115,13 @@ __device__ __forceinline__ void rope_kv_item(const RopeKvArgs& a, const PartialS
 // act = bf16(silu(bf16(gate)) * bf16(up)) from the gate/up partials, for the groups of
 // four consecutive elements e4 = first, first + stride, ... < rows * I / 4.
 __device__ __forceinline__ void swiglu_range(const PartialSet& ps, int rows, int I,
-                                             __nv_bfloat16* act, long first, long stride) {
+                                             __nv_bfloat16* act, long first, long stride,
+                                             const int* row_active = nullptr) {
   const long n4 = (long)rows * I / 4;
   for (long e4 = first; e4 < n4; e4 += stride) {
     const long e = e4 * 4;
     const int r = (int)(e / I), j = (int)(e % I);
+    if (row_active && !row_active[r]) continue;  // a padding row of the device loop
     const PsTile tg = ps_tile(ps, r, j, 0), tu = ps_tile(ps, r, j, 1);
     const float4 g4 = ps_sum4_nb<4>(tg);
     const float4 u4 = ps_sum4_nb<4>(tu);

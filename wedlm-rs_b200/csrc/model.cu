@@ -450,6 +450,8 @@ Status forward_body(wedlm_ctx* ctx, int B, int R, int RL, const int* d, const Me
             o_rb = ml.rb, o_lsrc = ml.lsrc, o_s0 = ml.s0, o_sr = ml.sr, o_sl = ml.sl, o_ss = ml.ss;
   (void)o_ss;
   std::vector<int> h_rows(h_rows_p, h_rows_p + B), h_len(h_len_p, h_len_p + B);
+  // device loop: its padding rows skip the row-wise kernels
+  const int* act = dev ? d + ml.act : nullptr;
 
   const long H = m->H;
   const int es = m->esz;
@@ -458,7 +460,7 @@ Status forward_body(wedlm_ctx* ctx, int B, int R, int RL, const int* d, const Me
 
   {
     const int ph = prof_begin(ctx, st);
-    Status se = run_embed(m->embed, m->dt, d + o_tok, R, m->H, m->V, m->h, err, st);
+    Status se = run_embed(m->embed, m->dt, d + o_tok, R, m->H, m->V, m->h, err, st, act);
     prof_end(ctx, st, ph, WedlmProfiler::kOther, 2.0 * R * m->H * es, 0, 1);
     WEDLM_TRY(se);
   }
@@ -528,6 +530,7 @@ Status forward_body(wedlm_ctx* ctx, int B, int R, int RL, const int* d, const Me
   rk.row_seq = d + o_rslot;
   rk.dst_pos = d + o_dst;
   rk.q_out = m->q;
+  rk.row_active = act;
 
   // One projection.  f32 models: CUDA-core GEMM with its epilogue.  bf16 models:
   // tcgen05 GEMM on the packed weights; `ps` != NULL selects slot mode (split-K partials
@@ -632,7 +635,8 @@ Status forward_body(wedlm_ctx* ctx, int B, int R, int RL, const int* d, const Me
     // embed -> norm -> QKV of layer 0 -> RoPE; then per layer: attention, fused tail
     PartialSet ps;
     int ph = prof_begin(ctx, st);
-    WEDLM_TRY(other(run_resid_norm(m->h, nullptr, m->layers[0].ln1, R, m->H, m->eps, m->xn, st),
+    WEDLM_TRY(other(run_resid_norm(m->h, nullptr, m->layers[0].ln1, R, m->H, m->eps, m->xn, st,
+                                   act),
                     ph, norm_bytes));
     WEDLM_TRY(gemm(m->xn, H, m->layers[0].wqkv, nullptr, m->qkvdim, m->H, EPI_STORE_BF16, nullptr,
                    0, nullptr, 0, R, &ps));
@@ -686,7 +690,8 @@ Status forward_body(wedlm_ctx* ctx, int B, int R, int RL, const int* d, const Me
     // SwiGLU); the residual add and the following RMSNorm are one kernel.
     PartialSet ps;
     int ph = prof_begin(ctx, st);
-    WEDLM_TRY(other(run_resid_norm(m->h, nullptr, m->layers[0].ln1, R, m->H, m->eps, m->xn, st),
+    WEDLM_TRY(other(run_resid_norm(m->h, nullptr, m->layers[0].ln1, R, m->H, m->eps, m->xn, st,
+                                   act),
                     ph, norm_bytes));
     for (int l = 0; l < m->nlayers; ++l) {
       const LayerWeights& L = m->layers[l];
@@ -702,17 +707,19 @@ Status forward_body(wedlm_ctx* ctx, int B, int R, int RL, const int* d, const Me
       WEDLM_TRY(gemm(m->attn, m->qdim, L.wo, nullptr, m->H, m->qdim, EPI_STORE_BF16, nullptr, 0,
                      nullptr, 0, R, &ps));
       ph = prof_begin(ctx, st);
-      WEDLM_TRY(other(run_resid_norm(m->h, &ps, L.ln2, R, m->H, m->eps, m->xn, st), ph, 2 * norm_bytes));
+      WEDLM_TRY(other(run_resid_norm(m->h, &ps, L.ln2, R, m->H, m->eps, m->xn, st, act), ph,
+                      2 * norm_bytes));
       WEDLM_TRY(gemm(m->xn, H, L.wgate, L.wup, m->I, m->H, EPI_SWIGLU_BF16, nullptr, 0, nullptr, 0,
                      R, &ps));
       ph = prof_begin(ctx, st);
-      WEDLM_TRY(other(run_swiglu(ps, R, m->I, m->act, st), ph, (double)R * m->I * es));
+      WEDLM_TRY(other(run_swiglu(ps, R, m->I, m->act, st, act), ph, (double)R * m->I * es));
       WEDLM_TRY(gemm(m->act, m->I, L.wdown, nullptr, m->H, m->I, EPI_STORE_BF16, nullptr, 0,
                      nullptr, 0, R, &ps));
       // residual add + the next RMSNorm: next layer's input norm, or the final norm
       const float* wn = (l + 1 < m->nlayers) ? m->layers[l + 1].ln1 : m->final_norm;
       ph = prof_begin(ctx, st);
-      WEDLM_TRY(other(run_resid_norm(m->h, &ps, wn, R, m->H, m->eps, m->xn, st), ph, 2 * norm_bytes));
+      WEDLM_TRY(other(run_resid_norm(m->h, &ps, wn, R, m->H, m->eps, m->xn, st, act), ph,
+                      2 * norm_bytes));
     }
   } else {
     for (int l = 0; l < m->nlayers; ++l) {
@@ -836,7 +843,7 @@ Status model_forward_device(wedlm_ctx* ctx, const DeviceForward& df, void* logit
   const int B = df.B, R = df.B * df.W;
   WEDLM_CHECK_ARG(B >= 1 && B <= m->max_seqs && df.W >= 1, "bad device forward shape");
   WEDLM_CHECK_ARG(R <= m->max_rows, "more window rows than the context was created for");
-  WEDLM_CHECK_ARG((size_t)MetaLayout(R, B).total <= m->meta_ints, "metadata buffer too small");
+  WEDLM_CHECK_ARG((size_t)MetaLayout(R, B).total_dev <= m->meta_ints, "metadata buffer too small");
   WEDLM_CHECK_ARG(logits_dtype == m->dt || logits_dtype == WEDLM_F32,
                   "logits dtype must be the model dtype or F32");
   std::vector<int> h_rows(B, df.W);

@@ -36,10 +36,13 @@ struct MetaLayout {
                                               // slot, cache row, sequence, logit-row source
   int s0, sr, sl, ss;                         // [B] each: first row, attention rows (window
                                               // length), committed cache length, cache slot
-  int total;
+  int total;                                  // the fields above
+  int act, total_dev;                         // [R] device loop only: 1 = a window row,
+                                              // 0 = a padding row
   MetaLayout(int R, int B)
       : tok(0), pos(R), rank(2 * R), rslot(3 * R), dst(4 * R), rb(5 * R), lsrc(6 * R), s0(7 * R),
-        sr(7 * R + B), sl(7 * R + 2 * B), ss(7 * R + 3 * B), total(7 * R + 4 * B) {}
+        sr(7 * R + B), sl(7 * R + 2 * B), ss(7 * R + 3 * B), total(7 * R + 4 * B),
+        act(7 * R + 4 * B), total_dev(8 * R + 4 * B) {}
 };
 
 // A forward whose metadata a device kernel wrote into the model's metadata buffer (the
