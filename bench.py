@@ -870,6 +870,7 @@ def bench_decode_8b(args, rank, ws, local):
         "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: random-init N(0,0.02^2) 8B-shape weights, uniform random prompt ids",
         "config": {"workload": DECODE_8B_WORKLOAD,
+                   "decode_loop": args.decode_loop,
                    "layers": 36, "hidden": 4096, "heads": "32/8", "head_dim": 128,
                    "ffn": 12288, "vocab": 151936, "window": WINDOW_8B,
                    "tokens_per_step": round(toks / args.steps, 3),
@@ -1121,7 +1122,12 @@ def main():
                          "captures of the same kernels)")
     ap.add_argument("--profile", action="store_true",
                     help="short run for ncu: no load hold, no e2e, no CPU baseline")
+    ap.add_argument("--decode-loop", default="graph", choices=["graph", "device", "host"],
+                    help="decode session bookkeeping: on the device with one CUDA graph per "
+                         "step (default), on the device without the graph, or on the host")
     args = ap.parse_args()
+    os.environ["WEDLM_DEVICE_LOOP"] = "0" if args.decode_loop == "host" else "1"
+    os.environ["WEDLM_STEP_GRAPH"] = "1" if args.decode_loop == "graph" else "0"
     args.warmup = max(args.warmup, 3)
     if args.profile:
         args.hold_seconds, args.no_cpu_baseline = 0.0, True
