@@ -46,7 +46,8 @@ constexpr int kQT = 128;        // query rows per tile
 constexpr int kKC = 128;        // keys per chunk (two 64-key pages)
 constexpr int kD = 128;         // head dim (this kernel)
 constexpr int kBlk = 128 * 128; // bytes of one [128 rows x 64 bf16] K-block
-constexpr int kStages = 2;
+constexpr int kKStages = 3;  // K ring
+constexpr int kVStages = 2;  // V ring
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct AttnWork {
@@ -75,6 +76,21 @@ struct AtParams {
   const int* n_comb_dev;
 };
 
+// 32 consecutive 32-bit columns of this thread's TMEM lane (P as packed bf16 pairs).
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+      "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]),
+      "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
+      "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
@@ -89,16 +105,6 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) 
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-// byte offset of element (row, col) in a 128-byte-swizzled [rows x 64] bf16 K-block
-__device__ __forceinline__ uint32_t sw128_off(int row, int col) {
-  const int chunk = (col >> 3) ^ (row & 7);
-  return (uint32_t)(row * 128 + chunk * 16 + (col & 7) * 2);
-}
-
 __global__ void __launch_bounds__(kThreadsAT, 1)
 attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const AtParams p) {
@@ -109,24 +115,23 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  // layout: Q (2 blocks) | K stages (2 blocks each) | V stages (2 blocks each) | P (2 blocks)
-  //         | barriers (<= 14) | TMEM slot | ranks
+  // layout: Q (2 blocks) | K stages (2 blocks each) | V stages (2 blocks each)
+  //         | barriers (15) | TMEM slot | ranks      (P lives in tensor memory)
   uint8_t* sQ = smem;
   uint8_t* sK = sQ + 2 * kBlk;
-  uint8_t* sV = sK + kStages * 2 * kBlk;
-  uint8_t* sP = sV + kStages * 2 * kBlk;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kBlk);
+  uint8_t* sV = sK + kKStages * 2 * kBlk;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kVStages * 2 * kBlk);
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;           // [kStages]
-  uint64_t* k_empty = k_full + kStages;  // [kStages]
-  uint64_t* v_full = k_empty + kStages;  // [kStages]
-  uint64_t* v_empty = v_full + kStages;  // [kStages]
-  uint64_t* s_full = v_empty + kStages;  // [2]: S buffers
+  uint64_t* k_full = bars + 1;            // [kKStages]
+  uint64_t* k_empty = k_full + kKStages;  // [kKStages]
+  uint64_t* v_full = k_empty + kKStages;  // [kVStages]
+  uint64_t* v_empty = v_full + kVStages;  // [kVStages]
+  uint64_t* s_full = v_empty + kVStages;  // [2]: S buffers
   uint64_t* p_full = s_full + 2;
-  uint64_t* o_done = p_full + 1;
+  uint64_t* o_done = p_full + 1;          // bars + 14
   // fixed offsets after the barriers, so that s_krank (read as int4) stays 16-byte
-  // aligned: slot at byte 112, ranks from byte 128
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  // aligned: slot at byte 128, ranks from byte 144
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   int* s_rank = reinterpret_cast<int*>(tmem_slot + 4);  // window ranks of sequence b
   int* s_krank = s_rank + 4096;                          // key ranks of the current chunk
   float* s_red = reinterpret_cast<float*>(s_krank + kKC);  // [4][128]: row max / sum halves
@@ -141,9 +146,11 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
   for (int j = threadIdx.x; j < S; j += blockDim.x) s_rank[j] = p.rank ? p.rank[row0 + j] : j;
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kKStages; ++s) {
       mbar_init(k_full + s, 1);
       mbar_init(k_empty + s, 1);
+    }
+    for (int s = 0; s < kVStages; ++s) {
       mbar_init(v_full + s, 1);
       mbar_init(v_empty + s, 1);
     }
@@ -159,8 +166,9 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   // two S buffers (S of chunk i in buffer i % 2, so that the next chunk's QK^T runs while
-  // the softmax reads this one) and the O accumulator
-  const uint32_t tS = tmem, tO = tmem + 256;
+  // the softmax reads this one), the O accumulator, and two P buffers (bf16 pairs, 64
+  // columns each; P of chunk i in buffer i % 2), the A operand of PV
+  const uint32_t tS = tmem, tO = tmem + 256, tP = tmem + 384;
 
   if (warp == 0 || warp == 10) {
     if (lane == 0) {
@@ -168,6 +176,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
       const bool kside = warp == 0;
       uint64_t* full = kside ? k_full : v_full;
       uint64_t* empty = kside ? k_empty : v_empty;
+      const int nst = kside ? kKStages : kVStages;
       if (kside) {
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmK);
@@ -181,8 +190,8 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
       }
       int issued = 0;
       for (int i = 0; i < nchunks; ++i) {
-        const int s = i % kStages;
-        const uint32_t ph = (uint32_t)(i / kStages) & 1u;
+        const int s = i % nst;
+        const uint32_t ph = (uint32_t)(i / nst) & 1u;
         if (!mbar_wait(empty + s, ph ^ 1u, p.err, kErrAtKvEmpty)) break;
         issued = i + 1;
         uint8_t* st = (kside ? sK : sV) + s * 2 * kBlk;
@@ -203,37 +212,38 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
         }
       }
       if (kside) mbar_wait(q_full, 0, p.err, kErrAtDrainQ);
-      for (int s = 0; s < kStages && s < issued; ++s) {
-        const int last = s + ((issued - 1 - s) / kStages) * kStages;
-        mbar_wait(full + s, (uint32_t)(last / kStages) & 1u, p.err, kErrAtDrainKv);
+      for (int s = 0; s < nst && s < issued; ++s) {
+        const int last = s + ((issued - 1 - s) / nst) * nst;
+        mbar_wait(full + s, (uint32_t)(last / nst) & 1u, p.err, kErrAtDrainKv);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
       const uint32_t idesc = idesc_bf16_f32(128, 128);
-      const uint32_t aq = smem_u32(sQ), ap = smem_u32(sP);
+      const uint32_t aq = smem_u32(sQ);
       bool ok = mbar_wait(q_full, 0, p.err, kErrAtMmaQ);
-      // O += P(j) . V(j), once the softmax has published P(j) and V(j) has landed
+      // O += P(j) . V(j), once the softmax has published P(j) (in TMEM: keys 16 kk ..
+      // 16 kk + 15 in columns 8 kk .. 8 kk + 7) and V(j) has landed
       auto pv = [&](int j, int code) -> bool {
-        const int sv = j % kStages;
+        const int sv = j % kVStages;
         if (!mbar_wait(p_full, (uint32_t)j & 1u, p.err, code)) return false;
-        if (!mbar_wait(v_full + sv, (uint32_t)(j / kStages) & 1u, p.err, kErrAtMmaKv)) return false;
+        if (!mbar_wait(v_full + sv, (uint32_t)(j / kVStages) & 1u, p.err, kErrAtMmaKv)) return false;
         tc_fence_after();
         const uint32_t bv = smem_u32(sV + sv * 2 * kBlk);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          tc_mma_f16(tO, smem_desc_sw128(ap + (kk >> 2) * kBlk + (kk & 3) * 32),
-                     smem_desc_sw128(bv + (kk >> 2) * kBlk + (kk & 3) * 32), idesc,
-                     j > 0 || kk > 0);
+          tc_mma_f16_ts(tO, tP + (uint32_t)((j & 1) * 64 + kk * 8),
+                        smem_desc_sw128(bv + (kk >> 2) * kBlk + (kk & 3) * 32), idesc,
+                        j > 0 || kk > 0);
         tc_commit(o_done);
         tc_commit(v_empty + sv);
         return true;
       };
       bool all_pv = nchunks > 0;  // every PV issued (each commits o_done once)
       for (int i = 0; i < nchunks && ok; ++i) {
-        const int s = i % kStages;
-        if (!mbar_wait(k_full + s, (uint32_t)(i / kStages) & 1u, p.err, kErrAtMmaKv)) {
+        const int s = i % kKStages;
+        if (!mbar_wait(k_full + s, (uint32_t)(i / kKStages) & 1u, p.err, kErrAtMmaKv)) {
           ok = false;
           break;
         }
@@ -319,28 +329,28 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
       const float mn = fmaxf(m, cm);
       const float base = mn == -INFINITY ? 0.f : mn;
       float ps = 0.f;
-      // PV(i-1) must be complete before P is overwritten and O is rescaled
-      if (i > 0) ok = ok && mbar_wait(o_done, (uint32_t)(i - 1) & 1u, p.err, kErrAtSoftO);
-      tc_fence_after();
-      // P = 2^(s - max) as bf16 into K-block `half` of the swizzled K-major P tile
-      // (2^-inf = 0 for masked keys)
+      // P = 2^(s - max) as bf16 pairs into this half's 32 columns of P buffer i % 2 in the
+      // row's TMEM lane (2^-inf = 0 for masked keys).  The buffer's last reader, PV(i-2),
+      // completed before the previous iteration rescaled O, so this runs while PV(i-1)
+      // still accumulates.
+      {
+        uint32_t pk[32];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint32_t pk[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const __nv_bfloat162 h2 = __floats2bfloat162_rn(fast_exp2(sv[c * 8 + 2 * j] - base),
-                                                          fast_exp2(sv[c * 8 + 2 * j + 1] - base));
+        for (int j = 0; j < 32; ++j) {
+          const __nv_bfloat162 h2 = __floats2bfloat162_rn(fast_exp2(sv[2 * j] - base),
+                                                          fast_exp2(sv[2 * j + 1] - base));
           ps += __low2float(h2) + __high2float(h2);
           pk[j] = *reinterpret_cast<const uint32_t*>(&h2);
         }
-        *reinterpret_cast<uint4*>(sP + half * kBlk + sw128_off(qr, c * 8)) =
-            make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        tmem_st32u(tP + (uint32_t)((i & 1) * 64) + lane_off + (uint32_t)(half * 32), pk);
       }
       // the row's sum over both halves (first half + second half)
       s_red[(2 + half) * kQT + qr] = ps;
       named_bar_sync(1, kSoftThreads);
       ps = s_red[2 * kQT + qr] + s_red[3 * kQT + qr];
+      // PV(i-1) must be complete before O is rescaled (and PV(i) accumulates into it)
+      if (i > 0) ok = ok && mbar_wait(o_done, (uint32_t)(i - 1) & 1u, p.err, kErrAtSoftO);
+      tc_fence_after();
       // Rescale this half of the O row when its running max grew.  tcgen05.ld / st are
       // warp-wide (.sync.aligned), so the whole warp takes the branch when any of its rows
       // needs it; rows that do not keep the factor 1.
@@ -358,7 +368,6 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
       }
       l = (m == -INFINITY ? 0.f : l * fast_exp2(m - base)) + ps;
       m = mn;
-      fence_proxy_async_smem();
       tc_fence_before();
       ok = named_bar_and(1, kSoftThreads, ok);  // the eight warps leave the loop together
       if (warp == 2 && lane == 0) mbar_arrive(p_full);
@@ -726,7 +735,8 @@ Status run_attention_tc(const AttnArgs& a, const AttnPlan& plan, int* err, cudaS
   p.err = err;
   p.n_work_dev = plan.n_work_dev;
   p.n_comb_dev = plan.n_comb_dev;
-  const size_t smem = 1024 + (2 + kStages * 4 + 2) * kBlk + 16 * 8 + 4096 * 4 + kKC * 4 + 4 * kQT * 4;
+  const size_t smem =
+      1024 + (2 + kKStages * 2 + kVStages * 2) * kBlk + 18 * 8 + 4096 * 4 + kKC * 4 + 4 * kQT * 4;
   int dev = 0;
   WEDLM_CUDA_TRY(cudaGetDevice(&dev));
   static unsigned attr_set = 0;
