@@ -870,7 +870,8 @@ def bench_decode_8b(args, rank, ws, local):
         "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: random-init N(0,0.02^2) 8B-shape weights, uniform random prompt ids",
         "config": {"workload": DECODE_8B_WORKLOAD,
-                   "decode_loop": args.decode_loop,
+                   # a communicator keeps the host loop (its NCCL steps)
+                   "decode_loop": "host" if sharded else args.decode_loop,
                    "layers": 36, "hidden": 4096, "heads": "32/8", "head_dim": 128,
                    "ffn": 12288, "vocab": 151936, "window": WINDOW_8B,
                    "tokens_per_step": round(toks / args.steps, 3),
