@@ -133,6 +133,11 @@ __global__ void attention_f32_kernel(AttnArgs a) {
 }
 
 // ---- residual add (from split-K partials) fused with the next RMSNorm ----------------
+// The row stays in registers (two groups of four values per thread when H <= 8 *
+// blockDim), so the kernel needs no row buffer in shared memory and its CTAs fit on an SM
+// beside a GEMM CTA: they are resident, waiting for the GEMM, when it completes.  Wider
+// rows keep the row in dynamic shared memory.
+template <bool kRegs>
 __global__ void __launch_bounds__(512)
 resid_norm_kernel(__nv_bfloat16* h, PartialSet ps, int has_ps, const float* __restrict__ w,
                   int H, float eps, __nv_bfloat16* xn, const int* act) {
@@ -143,6 +148,7 @@ resid_norm_kernel(__nv_bfloat16* h, PartialSet ps, int has_ps, const float* __re
   if (act && !act[r]) return;  // a padding row of the device loop
   __nv_bfloat16* hr = h + (long)r * H;
   float ss = 0.f;
+  float keep[8];  // kRegs: this thread's values at i0 .. i0 + 3 and i1 .. i1 + 3
   // two float4 groups per iteration, every load of both issued before the arithmetic
   const int step = blockDim.x * 4;
   for (int i0 = threadIdx.x * 4; i0 < H; i0 += 2 * step) {
@@ -180,7 +186,8 @@ resid_norm_kernel(__nv_bfloat16* h, PartialSet ps, int has_ps, const float* __re
       }
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        srow[i + k] = v[k];
+        if (kRegs) keep[g * 4 + k] = v[k];
+        else srow[i + k] = v[k];
         ss = fmaf(v[k], v[k], ss);
       }
     }
@@ -197,11 +204,24 @@ resid_norm_kernel(__nv_bfloat16* h, PartialSet ps, int has_ps, const float* __re
   __syncthreads();
   const float denom = sqrtf(sh[0] / (float)H + eps);
   __nv_bfloat16* xr = xn + (long)r * H;
-  for (int i = threadIdx.x * 4; i < H; i += blockDim.x * 4) {
-    const __nv_bfloat162 a = __floats2bfloat162_rn((srow[i] / denom) * w[i], (srow[i + 1] / denom) * w[i + 1]);
-    const __nv_bfloat162 b = __floats2bfloat162_rn((srow[i + 2] / denom) * w[i + 2], (srow[i + 3] / denom) * w[i + 3]);
-    *reinterpret_cast<uint2*>(xr + i) =
-        make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+  if (kRegs) {
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+      const int i = threadIdx.x * 4 + g * step;
+      if (i >= H) break;
+      const float* v = keep + g * 4;
+      const __nv_bfloat162 a = __floats2bfloat162_rn((v[0] / denom) * w[i], (v[1] / denom) * w[i + 1]);
+      const __nv_bfloat162 b = __floats2bfloat162_rn((v[2] / denom) * w[i + 2], (v[3] / denom) * w[i + 3]);
+      *reinterpret_cast<uint2*>(xr + i) =
+          make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+    }
+  } else {
+    for (int i = threadIdx.x * 4; i < H; i += blockDim.x * 4) {
+      const __nv_bfloat162 a = __floats2bfloat162_rn((srow[i] / denom) * w[i], (srow[i + 1] / denom) * w[i + 1]);
+      const __nv_bfloat162 b = __floats2bfloat162_rn((srow[i + 2] / denom) * w[i + 2], (srow[i + 3] / denom) * w[i + 3]);
+      *reinterpret_cast<uint2*>(xr + i) =
+          make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+    }
   }
 }
 
@@ -221,9 +241,14 @@ Status run_resid_norm(void* h, const PartialSet* ps, const float* w, int rows, i
   if (rows == 0) return Status::ok();
   WEDLM_CHECK_ARG(H % 4 == 0, "hidden size must be a multiple of 4");
   const PartialSet p = ps ? *ps : PartialSet();
-  WEDLM_CUDA_TRY(launch_pdl(resid_norm_kernel, dim3(rows), dim3(512), (size_t)H * sizeof(float), st,
-                            (__nv_bfloat16*)h, p, ps ? 1 : 0, w, H, eps, (__nv_bfloat16*)xn,
-                            row_active));
+  if (H <= 8 * 512)
+    WEDLM_CUDA_TRY(launch_pdl(resid_norm_kernel<true>, dim3(rows), dim3(512), 0, st,
+                              (__nv_bfloat16*)h, p, ps ? 1 : 0, w, H, eps, (__nv_bfloat16*)xn,
+                              row_active));
+  else
+    WEDLM_CUDA_TRY(launch_pdl(resid_norm_kernel<false>, dim3(rows), dim3(512),
+                              (size_t)H * sizeof(float), st, (__nv_bfloat16*)h, p, ps ? 1 : 0, w,
+                              H, eps, (__nv_bfloat16*)xn, row_active));
   return Status::ok();
 }
 
