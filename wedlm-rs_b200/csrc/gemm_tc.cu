@@ -373,6 +373,29 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
         } else {
           part = p.ws + (((long)cta * 2 + ((sg.it0 == beg) ? 0 : 1)) * p.nb + jn) * slot_floats;
         }
+        if (!(sg.full && !p.slot_mode)) {
+          // a partial: straight from TMEM, lane = weight row q * 32 + lane; for each token
+          // the warp's 32 lanes write 32 consecutive floats (one 128-byte run)
+          float* prow = part + q * 32 + lane;
+          for (int m = 0; m < na; ++m) {
+            float* pm = prow + (long)m * p.tok_tile * kTileN;
+            const uint32_t tm = trow + (uint32_t)(m * p.tok_tile);
+            for (int c = 0; c < p.tok_tile; c += 32) {
+              float v[32];
+              if (p.tok_tile - c >= 32) {
+                tmem_ld32(tm + (uint32_t)c, v);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) pm[(long)(c + j) * kTileN] = v[j];
+              } else {
+                float h[16];
+                tmem_ld16(tm + (uint32_t)c, h);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) pm[(long)(c + j) * kTileN] = h[j];
+              }
+            }
+          }
+          continue;
+        }
         float* tb = tbuf + (warp - 2) * (32 * 33);
         const int rr = q * 32 + (lane & 3) * 8;  // this lane's first weight row in the tile
         for (int c = 0; c < p.tok_tile; c += 32) {
@@ -384,19 +407,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
           for (int i = 0; i < 4; ++i) {
             const int tk = c + i * 8 + (lane >> 2);  // token within the tile
             if (i * 8 + (lane >> 2) >= w) continue;
-            if (sg.full && !p.slot_mode) {
-              if (ok && tk < tok_end) epilogue_store_vec<8>(p, t0 + tk, n0 + rr, o[i], o2[i]);
-            } else {
-              float* dst = part + (long)tk * kTileN + rr;
-              *reinterpret_cast<float4*>(dst) = make_float4(o[i][0], o[i][1], o[i][2], o[i][3]);
-              *reinterpret_cast<float4*>(dst + 4) = make_float4(o[i][4], o[i][5], o[i][6], o[i][7]);
-              if (p.dual) {
-                float* dst2 = part + (long)(p.tok_tile + tk) * kTileN + rr;
-                *reinterpret_cast<float4*>(dst2) = make_float4(o2[i][0], o2[i][1], o2[i][2], o2[i][3]);
-                *reinterpret_cast<float4*>(dst2 + 4) =
-                    make_float4(o2[i][4], o2[i][5], o2[i][6], o2[i][7]);
-              }
-            }
+            // a whole unit of direct mode: the final epilogue, 8 weight rows per lane
+            if (ok && tk < tok_end) epilogue_store_vec<8>(p, t0 + tk, n0 + rr, o[i], o2[i]);
           }
         }
       }
