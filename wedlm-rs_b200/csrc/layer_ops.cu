@@ -134,9 +134,10 @@ __global__ void attention_f32_kernel(AttnArgs a) {
 
 // ---- residual add (from split-K partials) fused with the next RMSNorm ----------------
 // The row stays in registers (two groups of four values per thread when H <= 8 *
-// blockDim), so the kernel needs no row buffer in shared memory and its CTAs fit on an SM
-// beside a GEMM CTA: they are resident, waiting for the GEMM, when it completes.  Wider
-// rows keep the row in dynamic shared memory.
+// blockDim), so the kernel needs no row buffer in shared memory.  Wider rows keep the row
+// in dynamic shared memory.  At 68 registers a 512-thread CTA does not fit on an SM beside
+// a GEMM CTA (192 threads x 168 registers); making it fit, by holding this kernel to 64
+// registers or the GEMM to 144, made the 8B decode step 2% slower.
 template <bool kRegs>
 __global__ void __launch_bounds__(512)
 resid_norm_kernel(__nv_bfloat16* h, PartialSet ps, int has_ps, const float* __restrict__ w,
