@@ -14,7 +14,7 @@ logits.  At every step:
 
 * logits of the mask rows (LM head written as f32, i.e. before the final bf16
   rounding) against the bf16 oracle: max |err| <= LOGIT_MAX_ABS, mean <= LOGIT_MEAN.
-  The north-star figure of 2e-2 max-abs is below the rounding noise of bf16 itself at
+  A 2e-2 max-abs logit bound is below the rounding noise of bf16 itself at
   these widths: the bf16 oracle differs from the exact f32 computation by ~0.1 max-abs
   on the same weights (module constants), so no bf16 implementation that rounds where
   the reference rounds can be held to 2e-2;

@@ -1,6 +1,6 @@
 """Parity of the fused entropy-select kernel (through the C ABI) with the oracle.
 
-Tolerances: entropy 1e-3 absolute (bf16 logits), 2e-5 relative
+Tolerances: entropy 1e-3 absolute (bf16 logits; the parity bar), 2e-5 relative
 for f32 logits; max-prob 1e-4 relative; argmax and the committed selection bit-exact.
 The selection is checked twice: the oracle's rule applied to the kernel's own
 entropies must reproduce the kernel's selection exactly, and the oracle's rule on

@@ -1,6 +1,6 @@
 """The block forward and the streaming decode (through the C ABI) against the oracle.
 
-Tolerances (from the north-star parity bar):
+Tolerances (from the parity bar):
   f32 model: logits within 1e-4 relative (to max |logit|); committed ids and
              positions bit-exact at temperature 0.
   bf16 model: logits compared before the final bf16 rounding (LM head written as f32)
