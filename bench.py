@@ -838,6 +838,16 @@ def bench_decode_8b(args, rank, ws, local):
         dist.all_reduce(t)
         e2e_tok, e2e_steps = float(t[0].item()), float(t[1].item()) / ws
     steps_timed = max(n1 - n0, 1)
+    # the e2e call's own host<->device copies, counted by the session: the begin / step /
+    # result sequence that wedlm_generate_streaming runs, once more with its counters read
+    # (prompt ids and the loop's set-up in, one flag per step and the ids out)
+    ctx.decode_begin([0], prompt, NEW_8B, WINDOW_8B, params)
+    while ctx.decode_step(1 << 30) > 0:
+        pass
+    ctx.decode_result(0)
+    call_steps, call_h2d, call_d2h = ctx.decode_io_bytes()
+    ctx.decode_end()
+    call_steps = max(call_steps, 1)
 
     # the reference benchmark's comparison: autoregressive decoding on the same model
     # (engine.rs:160-217), one token per forward at the cached prompt (it needs the whole
@@ -883,8 +893,12 @@ def bench_decode_8b(args, rank, ws, local):
                                    f"dp{ws} (one independent sequence per GPU)")},
         "clocks": clocks,
         "e2e": {"value": round(e2e_tok / e2e_s, 2), "unit": "committed tok/s",
-                "h2d_bytes_per_step": int((h1 - h0) / steps_timed),
-                "d2h_bytes_per_step": int((d1 - d0) / steps_timed),
+                "h2d_bytes_per_step": round(call_h2d / call_steps, 1),
+                "d2h_bytes_per_step": round(call_d2h / call_steps, 1),
+                "bytes_per_call": {"h2d": int(call_h2d), "d2h": int(call_d2h),
+                                   "steps": int(call_steps)},
+                "timed_loop_bytes_per_step": {"h2d": round((h1 - h0) / steps_timed, 1),
+                                              "d2h": round((d1 - d0) / steps_timed, 1)},
                 "tokens": int(e2e_tok), "steps_per_sequence": round(e2e_steps, 1),
                 "runs_s": [round(r, 4) for r in runs], "of_runs": f"median of {E2E_CALLS} calls",
                 "clocks": e2e_clocks,
