@@ -722,6 +722,17 @@ DECODE_8B_WORKLOAD = ("decode_8b: 8B-shape WeDLM, 512-token prompt, 512 new toke
                       "balanced preset (tau 0.8, lambda 0.05, cap 8), T 0")
 
 
+def decode_8b_config(layers: int = 36) -> dict:
+    """The decode_8b workload, the ``config`` of both arms' lines: the model shape, the
+    prompt, the window and the preset.  How an arm runs it (decode loop, parallelism)
+    goes in top-level keys of its line."""
+    workload = DECODE_8B_WORKLOAD if layers == 36 else \
+        DECODE_8B_WORKLOAD + f" [reduced to {layers} layers]"
+    return {"workload": workload, "layers": layers, "hidden": 4096, "heads": "32/8",
+            "head_dim": 128, "ffn": 12288, "vocab": 151936, "window": WINDOW_8B,
+            "l2": "inputs larger than L2: every step streams all weights (15.1 GB in bf16)"}
+
+
 def balanced_params():
     from wedlm_b200 import SamplingParams
     return SamplingParams.preset("balanced", temperature=0.0)
@@ -881,16 +892,13 @@ def bench_decode_8b(args, rank, ws, local):
         "ms_per_step": round(ms_max, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: random-init N(0,0.02^2) 8B-shape weights, uniform random prompt ids",
-        "config": {"workload": DECODE_8B_WORKLOAD,
-                   # a communicator keeps the host loop (its NCCL steps)
-                   "decode_loop": "host" if sharded else args.decode_loop,
-                   "layers": 36, "hidden": 4096, "heads": "32/8", "head_dim": 128,
-                   "ffn": 12288, "vocab": 151936, "window": WINDOW_8B,
-                   "tokens_per_step": round(toks / args.steps, 3),
-                   "l2": "inputs larger than L2 (15.1 GB of weights streamed per step)",
-                   "parallelism": (f"dp{ws} sequences + LM head and entropy pass vocabulary-"
-                                   f"sharded over {ws} GPUs (NCCL all-gathers)" if sharded else
-                                   f"dp{ws} (one independent sequence per GPU)")},
+        "config": decode_8b_config(),
+        # a communicator keeps the host loop (its NCCL steps)
+        "decode_loop": "host" if sharded else args.decode_loop,
+        "parallelism": (f"dp{ws} sequences + LM head and entropy pass vocabulary-sharded "
+                        f"over {ws} GPUs (NCCL all-gathers)" if sharded else
+                        f"dp{ws} (one independent sequence per GPU)"),
+        "tokens_per_step": round(toks / args.steps, 3),
         "clocks": clocks,
         "e2e": {"value": round(e2e_tok / e2e_s, 2), "unit": "committed tok/s",
                 "h2d_bytes_per_step": round(call_h2d / call_steps, 1),
@@ -1007,10 +1015,11 @@ class HostDecodeRun:
         t0 = time.time()
         # one committed token per step here (random-init entropy >> tau): max_new tokens
         # take at least max_new + 1 iterations
-        dec.generate_streaming(prompt, warmup + steps + 1, WINDOW_8B,
-                               OSP(temperature=0.0, entropy_threshold=0.8,
-                                   distance_penalty=0.05, max_tokens_per_step=8))
+        _, stats = dec.generate_streaming(prompt, warmup + steps + 1, WINDOW_8B,
+                                          OSP(temperature=0.0, entropy_threshold=0.8,
+                                              distance_penalty=0.05, max_tokens_per_step=8))
         self.total_s = time.time() - t0
+        self.tokens_per_step = stats.tokens_generated / max(stats.steps, 1)
         st = self.starts
         n = min(steps, len(st) - 1 - warmup)
         return [st[warmup + i + 1] - st[warmup + i] for i in range(n)]
@@ -1091,14 +1100,13 @@ def reference_decode(args, rank, ws):
               f"LM head over all rows + entropy + selection + commit per step; numpy with "
               f"{run.threads} BLAS threads (weights drawn in {run.setup_s:.1f} s, loop "
               f"{run.total_s:.1f} s)")
-    workload = DECODE_8B_WORKLOAD if layers == 36 else \
-        DECODE_8B_WORKLOAD + f" [reduced to {layers} layers]"
     return {"metric": METRIC, "value": round(v, 4), "unit": "committed tok/s",
             "impl": "reference", "n_gpus": ws, "steps": len(steps), "warmup": args.warmup,
             "ms_per_step": round(step * 1e3, 1), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": workload, "layers": layers, "hidden": 4096, "heads": "32/8",
-                       "head_dim": 128, "ffn": 12288, "vocab": 151936, "window": WINDOW_8B},
+            "config": decode_8b_config(layers),
+            "parallelism": f"one host process, {run.threads} BLAS threads",
+            "tokens_per_step": round(run.tokens_per_step, 3),
             "cpu_baseline": {"value": round(v, 4), "unit": "committed tok/s",
                              "cores": run.threads, "kind": "port", "sample": sample},
             "e2e": {"value": round(v, 4), "unit": "committed tok/s", "h2d_bytes_per_step": 0,

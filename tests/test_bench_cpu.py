@@ -38,3 +38,6 @@ def test_reference_arm_line(workload, unit):
     assert cb["value"] == d["value"] and cb["kind"] in ("port", "reference")
     assert cb["cores"] >= 1 and cb["sample"]
     assert d["e2e"]["value"] == d["value"] and d["e2e"]["h2d_bytes_per_step"] == 0
+    if workload == "decode_8b":
+        # the B200 arm's line carries the same workload config (decode_8b_config())
+        assert d["config"] == bench.decode_8b_config(2)
